@@ -1,0 +1,451 @@
+"""Benchmark of the enumerate + sparse-coarsen SpMM hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 5|4|3|2|1]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+
+Default workload (config 5, the largest single-GPU configuration): A is
+16384 x 16384 fp32 at 95% sparsity (half the nonzeros in aligned 4x1
+vertical runs, half unstructured, N(0, 0.02^2)), coarsened with
+(kernel_m, kernel_n) = (4, 1); B is 16384 x 128 fp32 U(-1, 1), replicated.
+A step is one C = A*B.  With N GPUs, A is row-partitioned at row-panel
+boundaries (balanced by nonzeros), each rank multiplies its row block, and
+the C row blocks are gathered with NCCL all-gather (strong scaling: the job's
+work is fixed).
+
+Metric: GFLOP/s = 2*nnz*N / time (whole job), time = max over ranks of the
+CUDA-event time of the K timed steps; L2 (126 MB) is flushed before every
+timed step by writing a 256 MiB buffer outside the timed events.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HBM_FALLBACK_GBS = 6650.0
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "dram_traffic.json")
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", type=int, default=5, choices=[1, 2, 3, 4, 5])
+    p.add_argument("--n-cols-b", type=int, default=None)
+    p.add_argument("--kernel-m", type=int, default=4)
+    p.add_argument("--kernel-n", type=int, default=1)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="target CPU work of the bounded cpu_baseline sample")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------- inputs --
+
+def workload(cfg: int, n_cols_b):
+    """Returns (name, [(csr arrays, B)], kernel shapes) for the chosen config."""
+    from sparse_computation_b200 import workloads as wl
+    if cfg == 5:
+        N = n_cols_b or 128
+        a, B = wl.config5(n_cols_b=N)
+        return "config5: A 16384x16384 fp32 95% sparse (half 4x1 runs), B 16384x%d" % N, [(a, B)]
+    if cfg == 1:
+        a, B = wl.config1()
+        return "config1: A 512x512 p=0.10, B 512x32", [(a, B)]
+    if cfg == 2:
+        N = n_cols_b or 4
+        a, B = wl.config2(0.9, N)
+        return f"config2: A 512x512 90% magnitude-pruned, B 512x{N}", [(a, B)]
+    if cfg == 3:
+        N = n_cols_b or 128
+        return f"config3: A 2048x512 + 512x2048 90% Beta(2,18) rows, B Kx{N}", \
+            [wl.config3((2048, 512), N), wl.config3((512, 2048), N)]
+    N = n_cols_b or 128
+    return f"config4: 96-matrix transformer-base stack 80%, B Kx{N}", [(a, B) for _, a, B in wl.config4(N)]
+
+
+def row_slice(a, r0, r1):
+    m, n, ip, ix, dx = a
+    s, e = ip[r0], ip[r1]
+    return r1 - r0, n, (ip[r0:r1 + 1] - s).astype(np.int32), ix[s:e], dx[s:e]
+
+
+def balanced_panel_cuts(indptr, m_rows, km, world):
+    """Row-panel boundaries splitting the nonzeros into `world` near-equal shares."""
+    panels = (m_rows + km - 1) // km
+    ends = np.minimum(np.arange(1, panels + 1) * km, m_rows)
+    cum = indptr[ends].astype(np.int64)
+    total = cum[-1] if panels else 0
+    cuts = [0]
+    for r in range(1, world):
+        cuts.append(int(np.searchsorted(cum, total * r / world)) + 1 if total else panels * r // world)
+    cuts.append(panels)
+    cuts = [min(max(c, 0), panels) for c in cuts]
+    for i in range(1, len(cuts)):
+        cuts[i] = max(cuts[i], cuts[i - 1])
+    return cuts
+
+
+# ---------------------------------------------------------------- clocks --
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons every 200 ms."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def measured_peak_hbm():
+    try:
+        with open(PEAKS_FILE) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+def measured_traffic(workload_key):
+    try:
+        with open(TRAFFIC_FILE) as f:
+            return json.load(f).get(workload_key)
+    except Exception:
+        return None
+
+
+# ----------------------------------------------------------- CPU leg ----
+
+def cpu_reference_rate(mats, seconds, threads):
+    """Times the reference's spmm_csr_float (oracle/_ref, else the restated
+    oracle) on a bounded row sample of the workload; returns (GFLOP/s, kind,
+    sample description, threads)."""
+    from oracle import cpu
+    kind = "reference" if cpu.ref_available("libref_spmm.so") else "port"
+    fn = cpu.ref_spmm_csr_float if kind == "reference" else None
+    a, B = mats[0]
+    m, n, ip, ix, dx = a
+    ip32 = np.ascontiguousarray(ip, np.int32)
+    ix32 = np.ascontiguousarray(ix, np.int32)
+    dx32 = np.ascontiguousarray(dx, np.float32)
+    N = B.shape[1]
+    C = np.zeros((m, N), np.float32)
+
+    def run_rows(r0, r1):
+        if kind == "reference":
+            fn(ip32, ix32, dx32, B, C, r0, r1)
+        else:
+            s = row_slice(a, r0, r1)
+            cpu.spmm_csr_float(s[2], s[3], s[4], B, C[r0:r1])
+
+    # Each thread walks 512-row blocks (thread t takes blocks t, t+T, ...,
+    # wrapping around the matrix) until the deadline; the sample is what got
+    # done in `seconds`.
+    blk = 512
+    nblk = (m + blk - 1) // blk
+    done = [0] * threads
+    deadline = time.perf_counter() + seconds
+
+    def worker(t):
+        b = t
+        while time.perf_counter() < deadline:
+            r0 = (b % nblk) * blk
+            r1 = min(m, r0 + blk)
+            run_rows(r0, r1)
+            done[t] += int(ip[r1] - ip[r0])
+            b += threads
+
+    from concurrent.futures import ThreadPoolExecutor
+    t0 = time.perf_counter()
+    if threads == 1:
+        worker(0)
+    else:
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(worker, range(threads)))
+    dt = time.perf_counter() - t0
+    nnz = sum(done)
+    gflops = 2.0 * nnz * N / dt / 1e9
+    sample = (f"{nnz} nonzeros x N={N} in {dt:.2f} s: 512-row blocks of the {m}-row matrix "
+              f"({len(ix)} nnz) visited in order")
+    return gflops, kind, sample, dt
+
+
+# ----------------------------------------------------------- reference ---
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    name, mats = workload(args.config, args.n_cols_b)
+    threads = len(os.sched_getaffinity(0))
+    total_nnz = sum(len(a[3]) for a, _ in mats)
+    N = mats[0][1].shape[1]
+    # each step: a bounded sample (~0.25 s of all-core work)
+    vals = []
+    kind = sample = None
+    for i in range(args.warmup + args.steps):
+        g, kind, sample, dt = cpu_reference_rate(mats, 0.25, threads)
+        if i >= args.warmup:
+            vals.append(g)
+    v = statistics.median(vals)
+    line = {"metric": "SpMM GFLOP/s (2*nnz*N)", "value": v, "unit": "GFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 2.0 * total_nnz * N / (v * 1e9) * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded)", "impl": "reference",
+            "config": {"workload": name, "coarsening": None, "n_cols_b": N},
+            "cpu_baseline": {"value": v, "unit": "GFLOP/s", "cores": threads, "kind": kind,
+                             "sample": sample + f"; spmm_csr_float on {threads} threads over row blocks"},
+            "e2e": {"value": v, "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ ours --
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import sparse_computation_b200 as sc
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", device_id=dev)
+
+    name, mats = workload(args.config, args.n_cols_b)
+    km, kn = args.kernel_m, args.kernel_n
+    N = mats[0][1].shape[1]
+
+    # ---- setup: this rank's row blocks, coarsening, plans (untimed)
+    t_setup = time.perf_counter()
+    jobs = []  # (plan, B device, C block view, rows, global row offset, nnz)
+    total_nnz = 0
+    for a, B in mats:
+        m = a[0]
+        total_nnz += len(a[3])
+        cuts = balanced_panel_cuts(a[2], m, km, world)
+        p0, p1 = cuts[rank], cuts[rank + 1]
+        r0, r1 = min(p0 * km, m), min(p1 * km, m)
+        blk = row_slice(a, r0, r1)
+        cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*blk), km, kn)
+        plan = sc.SpMMPlan(cf, N, device=local)
+        max_rows = max(min(cuts[r + 1] * km, m) - min(cuts[r] * km, m) for r in range(world))
+        jobs.append({"plan": plan, "B": torch.from_numpy(B).to(dev), "rows": r1 - r0, "max_rows": max_rows,
+                     "m": m, "nnz_local": len(blk[3]), "Bhost": B, "cuts": cuts})
+    t_setup = time.perf_counter() - t_setup
+    for j in jobs:
+        j["gather"] = torch.empty((world, j["max_rows"], N), device=dev)
+        j["C"] = j["gather"][rank, : j["rows"]] if world > 1 else torch.empty((j["rows"], N), device=dev)
+
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        for j in jobs:
+            j["plan"].spmm(j["B"], j["C"], stream=stream)
+        if world > 1:
+            for j in jobs:
+                # in place: this rank's block already sits at its slot
+                dist.all_gather_into_tensor(j["gather"], j["gather"][rank])
+
+    kernel_events = []
+
+    with ClockSampler(local) as clocks:
+        for _ in range(args.warmup):
+            flush.zero_()
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        kstarts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        kends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            kstarts[i].record(stream)
+            for j in jobs:
+                j["plan"].spmm(j["B"], j["C"], stream=stream)
+            kends[i].record(stream)
+            if world > 1:
+                for j in jobs:
+                    dist.all_gather_into_tensor(j["gather"], j["gather"][rank])
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+        kern_ms = sum(s.elapsed_time(e) for s, e in zip(kstarts, kends)) / args.steps
+
+        # ---- e2e: host B -> device, product, gather, C -> host
+        e2e_steps = max(10, min(args.steps, 50))
+        if world == 1 and len(jobs) == 1:
+            j = jobs[0]
+            hB = torch.from_numpy(j["Bhost"]).pin_memory()
+            hC = torch.empty((j["rows"], N), dtype=torch.float32).pin_memory()
+            hBn, hCn = hB.numpy(), hC.numpy()
+            for _ in range(3):
+                j["plan"].spmm_host(hBn, hCn, stream=stream)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(e2e_steps):
+                j["plan"].spmm_host(hBn, hCn, stream=stream)  # sc_spmm_host: H2D, kernel, D2H, sync
+            e2e_s = (time.perf_counter() - t0) / e2e_steps
+            h2d = j["Bhost"].nbytes
+            d2h = hC.numel() * 4
+        else:
+            hBs = [torch.from_numpy(j["Bhost"]).pin_memory() for j in jobs]
+            hCs = [torch.empty((j["m"], N), dtype=torch.float32).pin_memory() for j in jobs]
+
+            def e2e_step():
+                for j, hB in zip(jobs, hBs):
+                    j["B"].copy_(hB, non_blocking=True)
+                    j["plan"].spmm(j["B"], j["C"], stream=stream)
+                if world > 1:
+                    for j in jobs:
+                        dist.all_gather_into_tensor(j["gather"], j["gather"][rank])
+                if rank == 0:
+                    for j, hC in zip(jobs, hCs):
+                        for r in range(world):
+                            a0 = min(j["cuts"][r] * km, j["m"])
+                            a1 = min(j["cuts"][r + 1] * km, j["m"])
+                            src = j["gather"][r, : a1 - a0] if world > 1 else j["C"]
+                            hC[a0:a1].copy_(src, non_blocking=True)
+                torch.cuda.synchronize()
+
+            for _ in range(3):
+                e2e_step()
+            if world > 1:
+                dist.barrier()
+            t0 = time.perf_counter()
+            for _ in range(e2e_steps):
+                e2e_step()
+            e2e_s = (time.perf_counter() - t0) / e2e_steps
+            h2d = sum(j["Bhost"].nbytes for j in jobs)
+            d2h = sum(j["m"] * N * 4 for j in jobs) if rank == 0 else 0
+
+    # ---- reduce over ranks (max time)
+    t = torch.tensor([step_ms, kern_ms, e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, kern_ms, e2e_s = t.tolist()
+    flops = 2.0 * total_nnz * N
+    ms_per_step = step_ms / args.steps
+    value = flops / (ms_per_step * 1e-3) / 1e9
+    e2e_value = flops / e2e_s / 1e9
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # ---- roofline of the dominant kernel (the SpMM launch of this rank)
+    K = mats[0][0][1]
+    M = mats[0][0][0]
+    if world == 1:
+        alg_bytes = sum(4.0 * len(a[3]) + 4.0 * a[1] * N + 4.0 * a[0] * N for a, _ in mats)
+    else:
+        j = jobs[0]
+        alg_bytes = 4.0 * j["nnz_local"] + 4.0 * K * N + 4.0 * j["rows"] * N
+    peak, peak_kind = measured_peak_hbm()
+    achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
+    props = torch.cuda.get_device_properties(dev)
+    clk = clocks.summary()
+    sm_max = clk["sm_max_mhz"] or 1965.0
+    fp32_peak = props.multi_processor_count * 128 * 2 * sm_max * 1e6 / 1e12
+    local_flops = 2.0 * sum(j["nnz_local"] for j in jobs) * N
+    traffic = measured_traffic(f"config{args.config}_n{N}_m{km}_{kn}_gpus{world}")
+    info = jobs[0]["plan"].info
+
+    line = {
+        "metric": "SpMM GFLOP/s (2*nnz*N)", "value": value, "unit": "GFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": name, "coarsening": [km, kn], "n_cols_b": N, "nnz": total_nnz,
+                   "parallelism": f"row-partition x{world} + NCCL all-gather of C" if world > 1 else "1 GPU",
+                   "l2": "flushed before every timed step (256 MiB write, outside the events)",
+                   "plan": {k: info[k] for k in ("entries", "items", "kernel", "warps_per_panel",
+                                                 "device_bytes")}},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic,
+                     "kernel_us": kern_ms * 1e3,
+                     "algorithmic_bytes": alg_bytes,
+                     "fp32_tflops": local_flops / (kern_ms * 1e-3) / 1e12,
+                     "fp32_peak_tflops": fp32_peak,
+                     "fp32_frac": local_flops / (kern_ms * 1e-3) / 1e12 / fp32_peak},
+        "e2e": {"value": e2e_value, "unit": "GFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_s * 1e3},
+        "gpu_launches": args.steps * len(jobs),
+        "clocks": clk,
+        "setup_s": t_setup,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        g, kind, sample, dt = cpu_reference_rate(mats, args.cpu_seconds, 1)
+        line["cpu_baseline"] = {"value": g, "unit": "GFLOP/s", "cores": 1, "kind": kind,
+                                "sample": sample + "; serial spmm_csr_float as in the reference"}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,152 @@
+/*
+ * sc_b200.h — C ABI of the B200-native enumerate + sparse-coarsen SpMM/SpMV library.
+ *
+ * Every entry point returns an int status (SC_OK == 0) and never throws or exits;
+ * on failure sc_last_error_string() holds a one-line reason (thread-local).
+ * Handles are opaque.  No CUDA or torch types appear in the signatures: device
+ * buffers are plain pointers, streams are passed as void* (a cudaStream_t).
+ *
+ * Reference interfaces each group replaces (paths relative to the
+ * hosseinal/sparse-computation tree):
+ *   .mtx reading          utils/Sparse_io.cpp:48-82 (readCSRMatrixFromMTX) and
+ *                         aggregation/utils/sparse_io.cpp:278-402 (sym_lib)
+ *   .cfmtx reading        utils/Sparse_io.cpp:84-181 (readCFMTXFile),
+ *                         utils/Sparse_io.cpp:186-196 (loadCfmtxMatrices)
+ *   companion path        utils/Sparse_io.cpp:28-46 (companionMtxPathFromCFMTX)
+ *   enumerate + coarsen   code_gen/ss_format/format_generator.py:36-129
+ *   .cfmtx writing        code_gen/ss_format/format_generator.py:132-160
+ *   pattern dictionary    code_gen/pattern_utiles/pattern_dictionary.py:29-60
+ *   device upload         example_cuda/spmm_demo_gpu_utils.h:38-67,207-245
+ *   large-B SpMM launch   example_cuda/spmm_demo_gpu_utils.h:1357-1712
+ *   small-B SpMM launch   example_cuda/spmm_small_b_col_demo_gpu_utils.h:1061-2986,4911-5064
+ *   SpMV launch           example_cuda/spmv_demo_gpu_utils.h:632-952
+ */
+#ifndef SC_B200_H
+#define SC_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SC_OK 0
+#define SC_ERR_ARG 1         /* bad argument (null pointer, size out of range) */
+#define SC_ERR_IO 2          /* file cannot be opened / read / written */
+#define SC_ERR_FORMAT 3      /* malformed .mtx / .cfmtx / dictionary content */
+#define SC_ERR_CUDA 4        /* a CUDA runtime call failed */
+#define SC_ERR_UNSUPPORTED 5 /* valid input outside what this build handles */
+#define SC_ERR_NOMEM 6       /* host allocation failed */
+
+typedef struct sc_csr sc_csr;   /* CSR matrix, int32 indices, float64 values */
+typedef struct sc_cf sc_cf;     /* pattern-compressed ("CF") matrix, one block per pattern */
+typedef struct sc_plan sc_plan; /* device-resident CF matrix + schedule for one B width */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int sc_version(void);
+/* Reason for the last failed call on this thread ("" when none). */
+const char *sc_last_error_string(void);
+
+/* ---------------------------------------------------------------- CSR ---- */
+
+/* Reads a Matrix-Market coordinate file (real | integer | pattern,
+ * general | symmetric) into CSR with columns ascending inside each row.
+ * Replaces readCSRMatrixFromMTX (utils/Sparse_io.cpp:48-82). */
+int sc_mtx_load_csr(const char *mtx_path, sc_csr **out);
+/* Copies caller CSR arrays (rowptr has m+1 entries) into a new handle. */
+int sc_csr_create(int32_t m, int32_t n, int64_t nnz, const int32_t *rowptr,
+                  const int32_t *colind, const double *vals, sc_csr **out);
+int sc_csr_dims(const sc_csr *a, int32_t *m, int32_t *n, int64_t *nnz);
+/* Borrowed pointers, valid until sc_csr_free. */
+int sc_csr_arrays(const sc_csr *a, const int32_t **rowptr, const int32_t **colind,
+                  const double **vals);
+void sc_csr_free(sc_csr *a);
+
+/* ----------------------------------------------------------------- CF ---- */
+
+/* Parses a .cfmtx file. Values are parsed to float32 exactly as
+ * readCFMTXFile does (utils/Sparse_io.cpp:144-150); vector_length 0 in the
+ * header is reported as 1 (utils/Sparse_io.cpp:152-154). */
+int sc_cf_load(const char *cfmtx_path, sc_cf **out);
+/* Pattern enumeration + coarsening on the host, bit-exact with
+ * csr_to_compressed_format_converter / transform_row_panel
+ * (code_gen/ss_format/format_generator.py:36-129).  dict_path NULL (or
+ * "false") selects the default dictionary build_patterns_map(kernel_m, 1)
+ * (pattern_dictionary.py:29-37); otherwise it is read like
+ * read_pattern_dictionary (pattern_dictionary.py:49-60).  kernel_n == 0 means
+ * a column pack of 32 / popcount per pattern (format_generator.py:44-45).
+ * nthreads <= 0 uses every host core (row panels are independent). */
+int sc_cf_from_csr(const sc_csr *a, int32_t kernel_m, int32_t kernel_n,
+                   const char *dict_path, int32_t nthreads, sc_cf **out);
+/* Writes the text .cfmtx byte-identically to format_writer
+ * (format_generator.py:132-160) for a CF built by sc_cf_from_csr; a CF read
+ * by sc_cf_load is written back token for token. */
+int sc_cf_write(const sc_cf *cf, const char *path);
+int sc_cf_dims(const sc_cf *cf, int32_t *num_rows, int32_t *num_cols,
+               int32_t *kernel_m, int32_t *num_patterns, int32_t *vector_length);
+/* Header line i (0-based, file order): mask string (NUL-terminated, written
+ * into mask_out of capacity mask_cap) and pattern id. */
+int sc_cf_header_line(const sc_cf *cf, int32_t line, char *mask_out, int32_t mask_cap,
+                      int32_t *pattern_id);
+/* Sizes of the block of pattern `pattern_id` (body order): popcount of its
+ * mask, RPP length, CB length and value count. */
+int sc_cf_pattern_sizes(const sc_cf *cf, int32_t pattern_id, int32_t *popcount,
+                        int64_t *n_rpp, int64_t *n_cb, int64_t *n_vals);
+/* Borrowed pointers to the block (RPP, CB, float32 values). */
+int sc_cf_pattern_arrays(const sc_cf *cf, int32_t pattern_id, const int32_t **rpp,
+                         const int32_t **cb, const float **vals);
+/* Number of real (non-padding) nonzeros stored in the CF. */
+int sc_cf_real_nnz(const sc_cf *cf, int64_t *nnz);
+void sc_cf_free(sc_cf *cf);
+/* "<stem>-<m>-<n>.cfmtx" -> "<stem>.mtx" (utils/Sparse_io.cpp:28-46). */
+int sc_companion_mtx_path(const char *cfmtx_path, char *out, int32_t cap);
+
+/* --------------------------------------------------------------- plan ---- */
+
+/* Uploads the CF matrix to `device` and builds the schedule for products with
+ * a dense operand of n_cols_b columns (B is K x n_cols_b row-major).  Replaces
+ * allocateAndCopyMixedFormat (spmm_demo_gpu_utils.h:207-245) and the
+ * generated launch configuration.  kernel_m must be 1..6. */
+int sc_plan_create(const sc_cf *cf, int32_t n_cols_b, int32_t device, sc_plan **out);
+/* Same, restricted to row panels [panel_begin, panel_end): C rows
+ * [panel_begin*kernel_m, min(M, panel_end*kernel_m)) are produced, and the dC
+ * pointer given to sc_spmm addresses the first of them.  Used to row-partition
+ * one matrix across GPUs. */
+int sc_plan_create_panels(const sc_cf *cf, int32_t n_cols_b, int32_t device,
+                          int64_t panel_begin, int64_t panel_end, sc_plan **out);
+
+typedef struct sc_plan_info {
+  int64_t rows;          /* C rows this plan produces */
+  int64_t cols;          /* K (rows of B) */
+  int64_t n_cols_b;      /* N */
+  int64_t panels;        /* row panels in this plan */
+  int64_t kernel_m;
+  int64_t nnz;           /* real nonzeros (padding excluded) */
+  int64_t entries;       /* (panel, column) entries after dropping padding */
+  int64_t items;         /* scheduled work items */
+  int64_t device_bytes;  /* device memory held by the plan */
+  int32_t kernel;        /* 1 = small-B (N<=4) kernel, 2 = large-B kernel */
+  int32_t warps_per_panel;
+} sc_plan_info;
+int sc_plan_get_info(const sc_plan *p, sc_plan_info *info);
+
+/* C = A*B (accumulate == 0) or C += A*B (accumulate != 0), fp32, on `stream`
+ * (NULL = legacy default stream).  dB: K x N row-major with leading dimension
+ * ldb; dC: rows x N row-major with leading dimension ldc.  Asynchronous; only
+ * kernel launches, so it may be captured into a CUDA graph.  Replaces the
+ * reference kernels' C += A*B with atomics (which needed a zeroed C). */
+int sc_spmm(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc,
+            int32_t accumulate, void *stream);
+/* y = A*x or y += A*x (plan built with n_cols_b == 1). */
+int sc_spmv(sc_plan *p, const float *dx, float *dy, int32_t accumulate, void *stream);
+/* End-to-end product from HOST buffers: copies hB (K x N, dense row-major)
+ * to the device, runs sc_spmm, copies C back to hC (rows x N), and
+ * synchronizes `stream`.  Staging buffers are allocated on the first call and
+ * kept by the plan. */
+int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream);
+void sc_plan_free(sc_plan *p);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SC_B200_H */

@@ -1,0 +1,76 @@
+"""Builds libsc_b200.so in-tree for sm_100a (B200) with nvcc.
+
+    python -m sparse_computation_b200.build          # or build() from Python
+
+The library is self-contained (static CUDA runtime) and exports only the C
+ABI declared in include/sc_b200.h.  Objects go to _build/ (git-ignored).
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+BUILD = os.path.join(ROOT, "_build")
+LIB = os.path.join(PKG, "libsc_b200.so")
+
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+CXXFLAGS = ["-O3", "-std=c++17", "-fPIC", "-pthread", "-Wall", "-Wno-unused-function"]
+
+HOST_SOURCES = ["sc_host.cpp"]
+# (source, extra flags, object name): sc_inst.cu is compiled once per kernel_m.
+CUDA_SOURCES = [("sc_plan.cu", [], "sc_plan.cu.o")] + [
+    ("sc_inst.cu", [f"-DSC_KM={km}"], f"sc_inst_km{km}.cu.o") for km in range(1, 7)]
+
+
+def _run(cmd):
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("build failed:\n" + " ".join(cmd) + "\n" + r.stdout + r.stderr)
+    return r.stdout + r.stderr
+
+
+def _newer(target, deps):
+    if not os.path.exists(target):
+        return False
+    t = os.path.getmtime(target)
+    return all(os.path.getmtime(d) <= t for d in deps)
+
+
+def build(verbose: bool = False, force: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
+    headers.append(os.path.join(INCLUDE, "sc_b200.h"))
+    jobs, objs = [], []
+    for src in HOST_SOURCES:
+        s = os.path.join(CSRC, src)
+        o = os.path.join(BUILD, src + ".o")
+        objs.append(o)
+        if force or not _newer(o, [s] + headers):
+            jobs.append(["g++", *CXXFLAGS, "-I", INCLUDE, "-I", CSRC, "-c", s, "-o", o])
+    for src, extra, oname in CUDA_SOURCES:
+        s = os.path.join(CSRC, src)
+        o = os.path.join(BUILD, oname)
+        objs.append(o)
+        if force or not _newer(o, [s] + headers):
+            jobs.append([NVCC, *ARCH, "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
+                         "-Xptxas", "-v" if verbose else "-O3",
+                         *extra, "-I", INCLUDE, "-I", CSRC, "-c", s, "-o", o])
+    with ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
+        for out in ex.map(_run, jobs):
+            if verbose and out:
+                print(out)
+    if force or jobs or not _newer(LIB, objs):
+        _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-Xcompiler", "-fPIC", "-Xlinker",
+              "--exclude-libs,ALL", *objs, "-o", LIB, "-lpthread"])
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose="-v" in sys.argv, force="-f" in sys.argv))

@@ -1,0 +1,26 @@
+// Instantiates the kernels of one kernel_m (SC_KM, set by the build) so the
+// six instantiation sets compile in parallel.
+#include "sc_kernels.cuh"
+
+#ifndef SC_KM
+#error "SC_KM must be defined (1..6)"
+#endif
+
+#define SC_CAT2(a, b) a##b
+#define SC_CAT(a, b) SC_CAT2(a, b)
+
+sc::WideFn SC_CAT(sc_wide_kernel_km, SC_KM)(int vec) {
+  switch (vec) {
+    case 1: return sc::spmm_wide_kernel<SC_KM, 1>;
+    case 2: return sc::spmm_wide_kernel<SC_KM, 2>;
+    default: return sc::spmm_wide_kernel<SC_KM, 4>;
+  }
+}
+
+sc::NarrowFn SC_CAT(sc_narrow_kernel_km, SC_KM)(int nb) {
+  switch (nb) {
+    case 1: return sc::spmm_narrow_kernel<SC_KM, 1>;
+    case 2: return sc::spmm_narrow_kernel<SC_KM, 2>;
+    default: return sc::spmm_narrow_kernel<SC_KM, 4>;
+  }
+}

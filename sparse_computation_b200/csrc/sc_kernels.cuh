@@ -1,0 +1,372 @@
+// Pattern-specialised SpMM/SpMV kernels over the plan's device layout.
+//
+// Device layout (built by sc_plan.cu):
+//   recs      uint32 words.  One record per (row panel, column) entry of a
+//             pattern: [column, v_0 .. v_{P-1}, zero fill] with P the pattern
+//             popcount and a stride of 2 words (P == 1), 4 words (P <= 3) or
+//             8 words (P <= 7).  v_p is the value of the p-th set row of the
+//             mask.  Coarsening padding (zero values, repeated column) is
+//             dropped.  Every segment starts on a 16-byte boundary.
+//   items     int2 {record offset in words, mask | len << 16}: up to 32
+//             consecutive entries of one (panel, pattern) segment.
+//   item_ptr  items of local panel i are [item_ptr[i], item_ptr[i+1]).
+//   order     CTA -> panel map, heaviest panels first.
+//
+// One CTA owns one row panel (and, for wide B, one 32*VEC-column slice of C),
+// so C is written once, without atomics and without pre-zeroing; the result
+// does not depend on scheduling.  The reference instead launched one block
+// per (panel, pattern) pair and combined them with atomicAdd
+// (example_cuda/spmm_demo_gpu_utils.h:1411-1416).
+//
+// Specialisation: the mask of each item is dispatched (binary search over
+// compile-time masks) to a body instantiated for that exact mask, so the
+// rows it feeds are compile-time register indices -- the role of the
+// reference's generated PatternWith{m}NNZByRowPanel{P} functions
+// (code_gen/spmm/spmm_format_code_generator.py:121-223).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace sc {
+
+constexpr int kItemEntries = 32;
+
+__host__ __device__ constexpr int popc_c(int x) {
+  int c = 0;
+  for (; x; x >>= 1) c += x & 1;
+  return c;
+}
+__host__ __device__ constexpr int rec_stride(int p) { return p == 1 ? 2 : (p <= 3 ? 4 : 8); }
+// Row (panel-relative) of the p-th set bit of mask.  Loop-based so that it
+// inlines and folds to a constant once the caller's loops are unrolled.
+__host__ __device__ constexpr int nth_row(int mask, int p) {
+  for (int r = 0; r < 32; ++r)
+    if ((mask >> r) & 1) {
+      if (p == 0) return r;
+      --p;
+    }
+  return 0;
+}
+
+template <int VEC> struct VecT;
+template <> struct VecT<1> { using T = float; };
+template <> struct VecT<2> { using T = float2; };
+template <> struct VecT<4> { using T = float4; };
+
+template <int VEC>
+__device__ __forceinline__ void load_vec(const float *p, float (&out)[VEC]) {
+  if constexpr (VEC == 1) {
+    out[0] = __ldg(p);
+  } else if constexpr (VEC == 2) {
+    float2 t = __ldg(reinterpret_cast<const float2 *>(p));
+    out[0] = t.x; out[1] = t.y;
+  } else {
+    float4 t = __ldg(reinterpret_cast<const float4 *>(p));
+    out[0] = t.x; out[1] = t.y; out[2] = t.z; out[3] = t.w;
+  }
+}
+
+// Loads one record (column + P values) at `r`.
+template <int P>
+__device__ __forceinline__ void load_rec(const uint32_t *__restrict__ r, int &col, float (&v)[P]) {
+  constexpr int S = rec_stride(P);
+  if constexpr (S == 2) {
+    uint2 t = __ldg(reinterpret_cast<const uint2 *>(r));
+    col = (int)t.x; v[0] = __uint_as_float(t.y);
+  } else if constexpr (S == 4) {
+    uint4 t = __ldg(reinterpret_cast<const uint4 *>(r));
+    col = (int)t.x;
+    uint32_t w[3] = {t.y, t.z, t.w};
+#pragma unroll
+    for (int p = 0; p < P; ++p) v[p] = __uint_as_float(w[p]);
+  } else {
+    uint4 a = __ldg(reinterpret_cast<const uint4 *>(r));
+    uint4 b = __ldg(reinterpret_cast<const uint4 *>(r) + 1);
+    col = (int)a.x;
+    uint32_t w[7] = {a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int p = 0; p < P; ++p) v[p] = __uint_as_float(w[p]);
+  }
+}
+
+// ------------------------------------------------------------ wide B ------
+// One warp walks the entries of an item in order; lane l owns C columns
+// [col0, col0+VEC) with col0 = slice*32*VEC + l*VEC.  Per entry: one
+// warp-uniform record load, one coalesced VEC-wide load of the B row, and
+// P*VEC FMAs into the mask's rows.
+template <int KM, int MASK, int VEC>
+__device__ __forceinline__ void seg_wide(const uint32_t *__restrict__ rec, int len,
+                                         const float *__restrict__ Bcol, int64_t ldb, bool active,
+                                         float (&acc)[KM][VEC]) {
+  constexpr int P = popc_c(MASK);
+  constexpr int S = rec_stride(P);
+  constexpr int U = 4;
+  int e = 0;
+  for (; e + U <= len; e += U) {
+    int col[U];
+    float v[U][P];
+    float b[U][VEC];
+#pragma unroll
+    for (int u = 0; u < U; ++u) load_rec<P>(rec + (e + u) * S, col[u], v[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (active) load_vec<VEC>(Bcol + (int64_t)col[u] * ldb, b[u]);
+      else {
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) b[u][q] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) acc[nth_row(MASK, p)][q] = fmaf(v[u][p], b[u][q], acc[nth_row(MASK, p)][q]);
+  }
+  for (; e < len; ++e) {
+    int col;
+    float v[P];
+    float b[VEC];
+    load_rec<P>(rec + e * S, col, v);
+    if (active) load_vec<VEC>(Bcol + (int64_t)col * ldb, b);
+    else {
+#pragma unroll
+      for (int q = 0; q < VEC; ++q) b[q] = 0.f;
+    }
+#pragma unroll
+    for (int p = 0; p < P; ++p)
+#pragma unroll
+      for (int q = 0; q < VEC; ++q) acc[nth_row(MASK, p)][q] = fmaf(v[p], b[q], acc[nth_row(MASK, p)][q]);
+  }
+}
+
+template <int KM, int VEC, int LO, int HI>
+__device__ __forceinline__ void dispatch_wide(int mask, const uint32_t *__restrict__ rec, int len,
+                                              const float *__restrict__ Bcol, int64_t ldb, bool active,
+                                              float (&acc)[KM][VEC]) {
+  if constexpr (HI - LO == 1) {
+    seg_wide<KM, LO, VEC>(rec, len, Bcol, ldb, active, acc);
+  } else {
+    constexpr int MID = (LO + HI) / 2;
+    if (mask < MID) dispatch_wide<KM, VEC, LO, MID>(mask, rec, len, Bcol, ldb, active, acc);
+    else dispatch_wide<KM, VEC, MID, HI>(mask, rec, len, Bcol, ldb, active, acc);
+  }
+}
+
+template <int KM, int VEC>
+__global__ void __launch_bounds__(256)
+spmm_wide_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ items,
+                 const int32_t *__restrict__ item_ptr, const int32_t *__restrict__ order,
+                 const float *__restrict__ B, int64_t ldb, float *__restrict__ C, int64_t ldc,
+                 int64_t rows, int n_cols, int accumulate) {
+  extern __shared__ float red[];  // [warps-1][KM][32*VEC]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const int panel = order[blockIdx.x];
+  const int col0 = blockIdx.y * 32 * VEC + lane * VEC;
+  const bool active = col0 < n_cols;
+  const float *Bcol = B + col0;
+
+  float acc[KM][VEC];
+#pragma unroll
+  for (int k = 0; k < KM; ++k)
+#pragma unroll
+    for (int q = 0; q < VEC; ++q) acc[k][q] = 0.f;
+
+  const int it0 = item_ptr[panel], it1 = item_ptr[panel + 1];
+  for (int it = it0 + warp; it < it1; it += nw) {
+    const int2 item = __ldg(items + it);
+    const int mask = item.y & 0xffff;
+    const int len = item.y >> 16;
+    dispatch_wide<KM, VEC, 1, (1 << KM)>(mask, recs + (uint32_t)item.x, len, Bcol, ldb, active, acc);
+  }
+
+  if (nw > 1) {
+    if (warp > 0) {
+#pragma unroll
+      for (int k = 0; k < KM; ++k)
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) red[((warp - 1) * KM + k) * 32 * VEC + lane * VEC + q] = acc[k][q];
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    for (int w = 1; w < nw; ++w)
+#pragma unroll
+      for (int k = 0; k < KM; ++k)
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) acc[k][q] += red[((w - 1) * KM + k) * 32 * VEC + lane * VEC + q];
+  }
+  if (!active) return;
+#pragma unroll
+  for (int k = 0; k < KM; ++k) {
+    const int64_t row = (int64_t)panel * KM + k;
+    if (row >= rows) break;
+    float *c = C + row * ldc + col0;
+    if constexpr (VEC == 1) {
+      c[0] = accumulate ? c[0] + acc[k][0] : acc[k][0];
+    } else if constexpr (VEC == 2) {
+      float2 o = make_float2(acc[k][0], acc[k][1]);
+      if (accumulate) { float2 x = *reinterpret_cast<float2 *>(c); o.x += x.x; o.y += x.y; }
+      *reinterpret_cast<float2 *>(c) = o;
+    } else {
+      float4 o = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+      if (accumulate) {
+        float4 x = *reinterpret_cast<float4 *>(c);
+        o.x += x.x; o.y += x.y; o.z += x.z; o.w += x.w;
+      }
+      *reinterpret_cast<float4 *>(c) = o;
+    }
+  }
+}
+
+// ------------------------------------------------------------ narrow B ----
+// N in {1, 2, 4}: lane l takes entry l of an item (items hold <= 32
+// entries), multiplies the P values by the NB-wide B row, and keeps KM*NB
+// partial sums; a warp transpose-reduction then a cross-warp pass through
+// shared memory produce the panel's KM x NB block.  This replaces the
+// reference's lane-packed segmented shuffle reduction
+// (code_gen/spmm_small_b_col/spmm_small_b_col_format_code_generator.py:212-323).
+template <int KM, int MASK, int NB>
+__device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ rec, int len,
+                                           const float *__restrict__ B, int64_t ldb, int lane,
+                                           float (&acc)[KM][NB]) {
+  constexpr int P = popc_c(MASK);
+  constexpr int S = rec_stride(P);
+  if (lane < len) {
+    int col;
+    float v[P];
+    load_rec<P>(rec + lane * S, col, v);
+    float b[NB];
+    load_vec<NB>(B + (int64_t)col * ldb, b);
+#pragma unroll
+    for (int p = 0; p < P; ++p)
+#pragma unroll
+      for (int q = 0; q < NB; ++q) acc[nth_row(MASK, p)][q] = fmaf(v[p], b[q], acc[nth_row(MASK, p)][q]);
+  }
+}
+
+template <int KM, int NB, int LO, int HI>
+__device__ __forceinline__ void dispatch_narrow(int mask, const uint32_t *__restrict__ rec, int len,
+                                                const float *__restrict__ B, int64_t ldb, int lane,
+                                                float (&acc)[KM][NB]) {
+  if constexpr (HI - LO == 1) {
+    seg_narrow<KM, LO, NB>(rec, len, B, ldb, lane, acc);
+  } else {
+    constexpr int MID = (LO + HI) / 2;
+    if (mask < MID) dispatch_narrow<KM, NB, LO, MID>(mask, rec, len, B, ldb, lane, acc);
+    else dispatch_narrow<KM, NB, MID, HI>(mask, rec, len, B, ldb, lane, acc);
+  }
+}
+
+__host__ __device__ constexpr int pow2_ceil(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+__host__ __device__ constexpr int log2_c(int x) {
+  int l = 0;
+  while ((1 << l) < x) ++l;
+  return l;
+}
+
+// Reduces V (power of two <= 32) values across the warp with V-1 + 5-log2(V)
+// shuffles: at each halving step a lane keeps one half of its values and
+// sends the other half to its partner.  Afterwards v[0] of lane l is the
+// full sum of value index  sum_s bit(l, 4-s) * (V >> (s+1)).
+template <int V>
+__device__ __forceinline__ void warp_transpose_reduce(float (&v)[V], int lane) {
+  constexpr int L = log2_c(V);
+#pragma unroll
+  for (int s = 0; s < L; ++s) {
+    const int off = 16 >> s;
+    const bool upper = (lane & off) != 0;
+    const int half = V >> (s + 1);
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      float send = upper ? v[i] : v[i + half];
+      float keep = upper ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+#pragma unroll
+  for (int s = L; s < 5; ++s) v[0] += __shfl_xor_sync(0xffffffffu, v[0], 16 >> s);
+}
+
+template <int V>
+__device__ __forceinline__ int transpose_reduce_index(int lane) {
+  constexpr int L = log2_c(V);
+  int idx = 0;
+#pragma unroll
+  for (int s = 0; s < L; ++s)
+    if (lane & (16 >> s)) idx += V >> (s + 1);
+  return idx;
+}
+
+template <int KM, int NB>
+__global__ void __launch_bounds__(256)
+spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ items,
+                   const int32_t *__restrict__ item_ptr, const int32_t *__restrict__ order,
+                   const float *__restrict__ B, int64_t ldb, float *__restrict__ C, int64_t ldc,
+                   int64_t rows, int accumulate) {
+  constexpr int V = pow2_ceil(KM * NB);
+  static_assert(V <= 32, "KM*NB must not exceed 32");
+  __shared__ float red[8][V];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const int panel = order[blockIdx.x];
+
+  float acc[KM][NB];
+#pragma unroll
+  for (int k = 0; k < KM; ++k)
+#pragma unroll
+    for (int q = 0; q < NB; ++q) acc[k][q] = 0.f;
+
+  const int it0 = item_ptr[panel], it1 = item_ptr[panel + 1];
+  for (int it = it0 + warp; it < it1; it += nw) {
+    const int2 item = __ldg(items + it);
+    dispatch_narrow<KM, NB, 1, (1 << KM)>(item.y & 0xffff, recs + (uint32_t)item.x, item.y >> 16, B,
+                                          ldb, lane, acc);
+  }
+
+  float v[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) v[i] = (i < KM * NB) ? acc[i / NB][i % NB] : 0.f;
+  warp_transpose_reduce<V>(v, lane);
+  constexpr int kRep = 32 / V;  // lanes sharing one value index
+  if ((lane % kRep) == 0) red[warp][transpose_reduce_index<V>(lane)] = v[0];
+  __syncthreads();
+  if (threadIdx.x < KM * NB) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += red[w][threadIdx.x];
+    const int k = threadIdx.x / NB, q = threadIdx.x % NB;
+    const int64_t row = (int64_t)panel * KM + k;
+    if (row < rows) {
+      float *c = C + row * ldc + q;
+      *c = accumulate ? *c + s : s;
+    }
+  }
+}
+
+using WideFn = void (*)(const uint32_t *, const int2 *, const int32_t *, const int32_t *, const float *,
+                        int64_t, float *, int64_t, int64_t, int, int);
+using NarrowFn = void (*)(const uint32_t *, const int2 *, const int32_t *, const int32_t *, const float *,
+                          int64_t, float *, int64_t, int64_t, int);
+
+}  // namespace sc
+
+// Per-kernel_m kernel tables, defined in sc_inst.cu (one object per kernel_m).
+sc::WideFn sc_wide_kernel_km1(int vec);
+sc::WideFn sc_wide_kernel_km2(int vec);
+sc::WideFn sc_wide_kernel_km3(int vec);
+sc::WideFn sc_wide_kernel_km4(int vec);
+sc::WideFn sc_wide_kernel_km5(int vec);
+sc::WideFn sc_wide_kernel_km6(int vec);
+sc::NarrowFn sc_narrow_kernel_km1(int nb);
+sc::NarrowFn sc_narrow_kernel_km2(int nb);
+sc::NarrowFn sc_narrow_kernel_km3(int nb);
+sc::NarrowFn sc_narrow_kernel_km4(int nb);
+sc::NarrowFn sc_narrow_kernel_km5(int nb);
+sc::NarrowFn sc_narrow_kernel_km6(int nb);

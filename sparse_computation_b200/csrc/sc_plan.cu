@@ -1,0 +1,360 @@
+// Device half of libsc_b200.so: builds the plan (device layout + schedule)
+// from a CF matrix and launches the pattern-specialised kernels.
+//
+// Replaces the reference's device deep copy (allocateAndCopyMixedFormat,
+// example_cuda/spmm_demo_gpu_utils.h:207-245: one cudaMalloc/cudaMemcpy per
+// array and per pattern, pointer-of-pointers on the device) with one
+// contiguous allocation holding a flat record stream and a work list.
+
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "sc_internal.h"
+#include "sc_kernels.cuh"
+
+namespace {
+
+void require(bool cond, int code, const std::string &msg) {
+  if (!cond) throw sc_error(code, msg);
+}
+
+void cuda_check(cudaError_t e, const char *what) {
+  if (e != cudaSuccess)
+    throw sc_error(SC_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cuda_check(cudaGetDevice(&prev), "cudaGetDevice");
+    if (prev != dev) cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+  }
+  ~DeviceGuard() {
+    int cur;
+    if (cudaGetDevice(&cur) == cudaSuccess && cur != prev && prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+struct sc_plan {
+  int device = 0;
+  int64_t rows = 0, cols = 0, n = 0, panels = 0, km = 0;
+  int64_t nnz = 0, entries = 0, items = 0;
+  int kernel = 0;   // 1 narrow, 2 wide
+  int warps = 1;
+  int vec = 1;      // wide kernel column vector width
+  void *dev = nullptr;
+  size_t dev_bytes = 0;
+  const uint32_t *recs = nullptr;
+  const int2 *item_list = nullptr;
+  const int32_t *item_ptr = nullptr;
+  const int32_t *order = nullptr;
+  float *stage_b = nullptr, *stage_c = nullptr;
+  ~sc_plan() {
+    if (dev || stage_b || stage_c) {
+      int prev;
+      bool ok = cudaGetDevice(&prev) == cudaSuccess;
+      if (ok && prev != device) cudaSetDevice(device);
+      if (dev) cudaFree(dev);
+      if (stage_b) cudaFree(stage_b);
+      if (stage_c) cudaFree(stage_c);
+      if (ok && prev != device) cudaSetDevice(prev);
+    }
+  }
+};
+
+namespace {
+
+using sc::WideFn;
+using sc::NarrowFn;
+
+WideFn wide_kernel(int km, int vec) {
+  switch (km) {
+    case 1: return sc_wide_kernel_km1(vec);
+    case 2: return sc_wide_kernel_km2(vec);
+    case 3: return sc_wide_kernel_km3(vec);
+    case 4: return sc_wide_kernel_km4(vec);
+    case 5: return sc_wide_kernel_km5(vec);
+    default: return sc_wide_kernel_km6(vec);
+  }
+}
+
+NarrowFn narrow_kernel(int km, int nb) {
+  switch (km) {
+    case 1: return sc_narrow_kernel_km1(nb);
+    case 2: return sc_narrow_kernel_km2(nb);
+    case 3: return sc_narrow_kernel_km3(nb);
+    case 4: return sc_narrow_kernel_km4(nb);
+    case 5: return sc_narrow_kernel_km5(nb);
+    default: return sc_narrow_kernel_km6(nb);
+  }
+}
+
+int pow2_at_least(int64_t x) {
+  int p = 1;
+  while (p < x && p < (1 << 30)) p <<= 1;
+  return p;
+}
+
+constexpr int64_t kTargetWarps = 148 * 32;  // B200: 148 SMs, ~half of the 64 warp slots
+
+sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int64_t pe) {
+  const int km = cf.kernel_m;
+  require(km >= 1 && km <= 6, SC_ERR_UNSUPPORTED, "plans support kernel_m 1..6");
+  require(n >= 1, SC_ERR_ARG, "n_cols_b must be >= 1");
+  const int64_t total_panels = ((int64_t)cf.num_rows + km - 1) / km;
+  if (pb < 0) pb = 0;
+  if (pe < 0 || pe > total_panels) pe = total_panels;
+  require(pb <= pe, SC_ERR_ARG, "panel range is empty or reversed");
+  const int np = (int)cf.pats.size();
+
+  // Validate every block before anything reaches the device.
+  std::vector<int> rowbits(np, 0);
+  for (int g = 0; g < np; ++g) {
+    const sc_pattern &pt = cf.pats[g];
+    require((int)pt.mask.size() == km, SC_ERR_UNSUPPORTED,
+            "pattern mask length differs from kernel_m (custom dictionary)");
+    for (int j = 0; j < km; ++j)
+      if (pt.mask[j] == '1') rowbits[g] |= 1 << j;
+    require(pt.popcount >= 1 && pt.popcount == __builtin_popcount(rowbits[g]), SC_ERR_FORMAT,
+            "pattern mask must have at least one row");
+    require((int64_t)pt.rpp.size() == total_panels + 1, SC_ERR_FORMAT,
+            "row-panel pointer length differs from ceil(rows/kernel_m)+1");
+    require(pt.rpp[0] == 0, SC_ERR_FORMAT, "row-panel pointer must start at 0");
+    for (size_t i = 0; i + 1 < pt.rpp.size(); ++i)
+      require(pt.rpp[i] <= pt.rpp[i + 1], SC_ERR_FORMAT, "row-panel pointer must be non-decreasing");
+    require((size_t)pt.rpp.back() <= pt.cb.size(), SC_ERR_FORMAT, "row-panel pointer exceeds column list");
+    require((size_t)pt.rpp.back() * pt.popcount <= pt.vals.size(), SC_ERR_FORMAT,
+            "value list shorter than columns x popcount");
+    require(pt.pad.size() == pt.vals.size(), SC_ERR_FORMAT, "internal: pad flags missing");
+  }
+
+  auto plan = std::make_unique<sc_plan>();
+  plan->device = device;
+  plan->km = km;
+  plan->n = n;
+  plan->cols = cf.num_cols;
+  plan->panels = pe - pb;
+  plan->rows = std::max<int64_t>(0, std::min<int64_t>(cf.num_rows, pe * km) - pb * km);
+
+  std::vector<uint32_t> recs;
+  std::vector<int2> items;
+  std::vector<int32_t> item_ptr(plan->panels + 1, 0);
+  std::vector<int64_t> work(plan->panels, 0);
+  for (int64_t lp = 0; lp < plan->panels; ++lp) {
+    const int64_t gp = pb + lp;
+    for (int g = 0; g < np; ++g) {
+      const sc_pattern &pt = cf.pats[g];
+      const int P = pt.popcount;
+      const int S = sc::rec_stride(P);
+      int64_t seg_start = -1;
+      int64_t seg_len = 0;
+      auto close_items = [&]() {
+        for (int64_t e = 0; e < seg_len; e += sc::kItemEntries) {
+          int len = (int)std::min<int64_t>(sc::kItemEntries, seg_len - e);
+          int64_t off = seg_start + e * S;
+          require(off < (int64_t)UINT32_MAX / 2, SC_ERR_UNSUPPORTED, "record stream exceeds 8 GiB");
+          items.push_back(make_int2((int)off, rowbits[g] | (len << 16)));
+        }
+      };
+      for (int32_t j = pt.rpp[gp]; j < pt.rpp[gp + 1]; ++j) {
+        bool all_pad = true;
+        for (int p = 0; p < P; ++p) all_pad &= pt.pad[(size_t)j * P + p] != 0;
+        if (all_pad) continue;
+        const int32_t col = pt.cb[j];
+        require(col >= 0 && col < cf.num_cols, SC_ERR_FORMAT, "column index out of range in CF");
+        if (seg_start < 0) {
+          while (recs.size() % 4) recs.push_back(0);  // 16-byte aligned segment
+          seg_start = (int64_t)recs.size();
+        }
+        recs.push_back((uint32_t)col);
+        for (int p = 0; p < P; ++p) {
+          float v = pt.vals[(size_t)j * P + p];
+          uint32_t w;
+          memcpy(&w, &v, 4);
+          recs.push_back(w);
+          if (!pt.pad[(size_t)j * P + p]) plan->nnz++;
+        }
+        for (int p = 1 + P; p < S; ++p) recs.push_back(0);
+        seg_len++;
+        plan->entries++;
+        work[lp] += P + 2;
+      }
+      if (seg_len > 0) close_items();
+    }
+    item_ptr[lp + 1] = (int32_t)items.size();
+    work[lp] += 4 * (item_ptr[lp + 1] - item_ptr[lp]);
+  }
+  plan->items = (int64_t)items.size();
+  while (recs.size() % 4) recs.push_back(0);
+  if (recs.empty()) recs.assign(4, 0);
+
+  std::vector<int32_t> order(plan->panels);
+  for (int64_t i = 0; i < plan->panels; ++i) order[i] = (int32_t)i;
+  std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return work[a] > work[b]; });
+
+  // Kernel family and CTA shape.
+  int slices = 1;
+  if (n == 1 || n == 2 || n == 4) {
+    plan->kernel = 1;
+  } else {
+    plan->kernel = 2;
+    plan->vec = n >= 128 ? 4 : (n >= 64 ? 2 : 1);
+    slices = (int)((n + 32 * plan->vec - 1) / (32 * plan->vec));
+  }
+  {
+    int64_t units = std::max<int64_t>(1, plan->panels * slices);
+    int w = pow2_at_least((kTargetWarps + units - 1) / units);
+    int64_t avg_items = plan->panels ? (plan->items + plan->panels - 1) / plan->panels : 1;
+    w = std::min(w, pow2_at_least(std::max<int64_t>(1, avg_items)));
+    plan->warps = std::max(1, std::min(w, 8));
+  }
+
+  // One device allocation: recs | items | item_ptr | order.
+  DeviceGuard dg(device);
+  auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  const size_t b_recs = align(recs.size() * 4);
+  const size_t b_items = align(std::max<size_t>(1, items.size()) * sizeof(int2));
+  const size_t b_ptr = align(item_ptr.size() * 4);
+  const size_t b_order = align(std::max<size_t>(1, order.size()) * 4);
+  plan->dev_bytes = b_recs + b_items + b_ptr + b_order;
+  cuda_check(cudaMalloc(&plan->dev, plan->dev_bytes), "cudaMalloc(plan)");
+  char *base = static_cast<char *>(plan->dev);
+  plan->recs = reinterpret_cast<const uint32_t *>(base);
+  plan->item_list = reinterpret_cast<const int2 *>(base + b_recs);
+  plan->item_ptr = reinterpret_cast<const int32_t *>(base + b_recs + b_items);
+  plan->order = reinterpret_cast<const int32_t *>(base + b_recs + b_items + b_ptr);
+  cuda_check(cudaMemcpy(base, recs.data(), recs.size() * 4, cudaMemcpyHostToDevice), "upload records");
+  if (!items.empty())
+    cuda_check(cudaMemcpy(base + b_recs, items.data(), items.size() * sizeof(int2), cudaMemcpyHostToDevice),
+               "upload items");
+  cuda_check(cudaMemcpy(base + b_recs + b_items, item_ptr.data(), item_ptr.size() * 4, cudaMemcpyHostToDevice),
+             "upload item pointers");
+  if (!order.empty())
+    cuda_check(cudaMemcpy(base + b_recs + b_items + b_ptr, order.data(), order.size() * 4,
+                          cudaMemcpyHostToDevice),
+               "upload panel order");
+  return plan.release();
+}
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+void launch(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int accumulate,
+            cudaStream_t stream) {
+  require(B != nullptr && C != nullptr, SC_ERR_ARG, "null B or C");
+  require(ldb >= p->n && ldc >= p->n, SC_ERR_ARG, "leading dimension smaller than n_cols_b");
+  if (p->panels == 0) return;
+  DeviceGuard dg(p->device);
+  const int threads = 32 * p->warps;
+  const int nb = (int)p->n;
+  if (p->kernel == 1 && ldb % nb == 0 && aligned(B, 4 * nb)) {
+    NarrowFn fn = narrow_kernel((int)p->km, nb);
+    fn<<<dim3((unsigned)p->panels), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, p->order, B, ldb,
+                                                           C, ldc, p->rows, accumulate);
+  } else {
+    int vec = p->kernel == 2 ? p->vec : 1;
+    while (vec > 1 && !(p->n % vec == 0 && ldb % vec == 0 && ldc % vec == 0 && aligned(B, 4 * vec) &&
+                        aligned(C, 4 * vec)))
+      vec >>= 1;
+    const int slices = (int)((p->n + 32 * vec - 1) / (32 * vec));
+    WideFn fn = wide_kernel((int)p->km, vec);
+    const size_t smem = (size_t)(p->warps - 1) * p->km * 32 * vec * sizeof(float);
+    fn<<<dim3((unsigned)p->panels, slices), threads, smem, stream>>>(p->recs, p->item_list, p->item_ptr,
+                                                                     p->order, B, ldb, C, ldc, p->rows,
+                                                                     (int)p->n, accumulate);
+  }
+  cuda_check(cudaGetLastError(), "kernel launch");
+}
+
+}  // namespace
+
+#define SC_API_BEGIN try {
+#define SC_API_END                          \
+  }                                         \
+  catch (const sc_error &e) {               \
+    sc_set_error(e.what());                 \
+    return e.code;                          \
+  }                                         \
+  catch (const std::bad_alloc &) {          \
+    sc_set_error("host allocation failed"); \
+    return SC_ERR_NOMEM;                    \
+  }                                         \
+  catch (const std::exception &e) {         \
+    sc_set_error(e.what());                 \
+    return SC_ERR_ARG;                      \
+  }                                         \
+  return SC_OK;
+
+extern "C" {
+
+int sc_plan_create(const sc_cf *cf, int32_t n_cols_b, int32_t device, sc_plan **out) {
+  SC_API_BEGIN
+  require(cf != nullptr && out != nullptr, SC_ERR_ARG, "null argument");
+  *out = build_plan(*cf, n_cols_b, device, 0, -1);
+  SC_API_END
+}
+
+int sc_plan_create_panels(const sc_cf *cf, int32_t n_cols_b, int32_t device, int64_t panel_begin,
+                          int64_t panel_end, sc_plan **out) {
+  SC_API_BEGIN
+  require(cf != nullptr && out != nullptr, SC_ERR_ARG, "null argument");
+  require(panel_begin >= 0 && panel_end >= panel_begin, SC_ERR_ARG, "bad panel range");
+  *out = build_plan(*cf, n_cols_b, device, panel_begin, panel_end);
+  SC_API_END
+}
+
+int sc_plan_get_info(const sc_plan *p, sc_plan_info *info) {
+  SC_API_BEGIN
+  require(p != nullptr && info != nullptr, SC_ERR_ARG, "null argument");
+  info->rows = p->rows;
+  info->cols = p->cols;
+  info->n_cols_b = p->n;
+  info->panels = p->panels;
+  info->kernel_m = p->km;
+  info->nnz = p->nnz;
+  info->entries = p->entries;
+  info->items = p->items;
+  info->device_bytes = (int64_t)p->dev_bytes;
+  info->kernel = p->kernel;
+  info->warps_per_panel = p->warps;
+  SC_API_END
+}
+
+int sc_spmm(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc, int32_t accumulate, void *stream) {
+  SC_API_BEGIN
+  require(p != nullptr, SC_ERR_ARG, "null plan");
+  launch(p, dB, ldb, dC, ldc, accumulate, static_cast<cudaStream_t>(stream));
+  SC_API_END
+}
+
+int sc_spmv(sc_plan *p, const float *dx, float *dy, int32_t accumulate, void *stream) {
+  SC_API_BEGIN
+  require(p != nullptr, SC_ERR_ARG, "null plan");
+  require(p->n == 1, SC_ERR_ARG, "sc_spmv needs a plan built with n_cols_b == 1");
+  launch(p, dx, 1, dy, 1, accumulate, static_cast<cudaStream_t>(stream));
+  SC_API_END
+}
+
+int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream) {
+  SC_API_BEGIN
+  require(p != nullptr && hB != nullptr && hC != nullptr, SC_ERR_ARG, "null argument");
+  DeviceGuard dg(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t bb = (size_t)p->cols * p->n * sizeof(float);
+  const size_t cb = (size_t)p->rows * p->n * sizeof(float);
+  if (!p->stage_b) cuda_check(cudaMalloc(&p->stage_b, std::max<size_t>(bb, 16)), "cudaMalloc(B staging)");
+  if (!p->stage_c) cuda_check(cudaMalloc(&p->stage_c, std::max<size_t>(cb, 16)), "cudaMalloc(C staging)");
+  if (bb) cuda_check(cudaMemcpyAsync(p->stage_b, hB, bb, cudaMemcpyHostToDevice, s), "copy B to device");
+  launch(p, p->stage_b, p->n, p->stage_c, p->n, 0, s);
+  if (cb) cuda_check(cudaMemcpyAsync(hC, p->stage_c, cb, cudaMemcpyDeviceToHost, s), "copy C to host");
+  cuda_check(cudaStreamSynchronize(s), "stream synchronize");
+  SC_API_END
+}
+
+void sc_plan_free(sc_plan *p) { delete p; }
+
+}  // extern "C"

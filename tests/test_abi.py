@@ -1,0 +1,91 @@
+"""The C ABI library loads, exports exactly what include/sc_b200.h declares,
+and reports errors as status codes (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import sparse_computation_b200 as sc
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    text = open(os.path.join(ROOT, "include", "sc_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sc_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = ctypes.CDLL(sc.LIB_PATH)
+    decl = declared_symbols()
+    assert decl, "no declarations parsed"
+    missing = [s for s in decl if not hasattr(L, s)]
+    assert not missing, missing
+    assert sorted(decl) == sorted(sc.EXPORTED_SYMBOLS)
+
+
+def test_only_c_abi_is_exported():
+    out = os.popen(f"nm -D --defined-only {sc.LIB_PATH}").read().split("\n")
+    names = [l.split()[-1] for l in out if l.strip() and l.split()[1] in "TtWw"]
+    ours = [n for n in names if n.startswith("sc_")]
+    assert sorted(ours) == sorted(declared_symbols())
+
+
+def test_version_and_errors(tmp_path):
+    L = sc.lib()
+    assert L.sc_version() >= 100
+    with pytest.raises(sc.ScError) as e:
+        sc.read_cfmtx(tmp_path / "missing.cfmtx")
+    assert e.value.code == sc.SC_ERR_IO
+    assert "unable to open" in str(e.value)
+    bad = tmp_path / "bad.cfmtx"
+    bad.write_text("1 2 3\n")
+    with pytest.raises(sc.ScError) as e:
+        sc.read_cfmtx(bad)
+    assert e.value.code == sc.SC_ERR_FORMAT
+    trunc = tmp_path / "t.cfmtx"
+    trunc.write_text("4 4 2 3 1\n11 0 \n10 1 \n01 2 \n0 1 1\n")
+    with pytest.raises(sc.ScError) as e:
+        sc.read_cfmtx(trunc)
+    assert e.value.code == sc.SC_ERR_FORMAT
+
+
+def test_plan_fails_loudly_without_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    a = sc.CSR.from_arrays(4, 4, [0, 1, 1, 1, 1], [2], [1.0])
+    cf = sc.csr_to_compressed_format_converter(a, 2, 1)
+    with pytest.raises(sc.ScError) as e:
+        sc.SpMMPlan(cf, 32)
+    assert e.value.code == sc.SC_ERR_CUDA
+
+
+def test_plan_rejects_bad_cf_before_device():
+    """Validation happens on the host, before any CUDA call."""
+    a = sc.CSR.from_arrays(4, 4, [0, 1, 1, 1, 1], [2], [1.0])
+    cf = sc.csr_to_compressed_format_converter(a, 8, 1)  # kernel_m 8 > 6
+    with pytest.raises(sc.ScError) as e:
+        sc.SpMMPlan(cf, 32)
+    assert e.value.code == sc.SC_ERR_UNSUPPORTED
+
+
+def test_csr_create_validates():
+    with pytest.raises(sc.ScError):
+        sc.CSR.from_arrays(2, 2, [0, 2, 1], [0, 1], [1.0, 2.0])
+    with pytest.raises(sc.ScError):
+        sc.CSR.from_arrays(1, 2, [0, 2], [1, 0], [1.0, 2.0])  # unsorted
+    with pytest.raises(sc.ScError):
+        sc.CSR.from_arrays(1, 2, [0, 1], [5], [1.0])  # out of range
+
+
+def test_companion_path():
+    # utils/Sparse_io.cpp:28-46
+    assert sc.companion_mtx_path("dir/mat-4-8.cfmtx") == "dir/mat.mtx"
+    assert sc.companion_mtx_path("dir/my-mat-64-128.cfmtx") == "dir/my-mat.mtx"
+    assert sc.companion_mtx_path("mat.cfmtx") == "mat.mtx"
+    assert sc.companion_mtx_path("mat-4.cfmtx") == "mat-4.mtx"
+    assert sc.companion_mtx_path("-4.cfmtx") == "-4.mtx"
+    assert sc.companion_mtx_path(".cfmtx") == ".cfmtx"

@@ -1,0 +1,212 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle
+(restated spmm_csr_float / spmv_csr_float), under
+|dC_ij| <= 1e-5 * sum_k |A_ik * B_kj|, on the benchmark configurations at
+full size and on the golden fixtures written by the reference's converter."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import sparse_computation_b200 as sc
+from oracle import cpu
+from parity import RTOL, assert_parity, to_csr_handle
+from sparse_computation_b200 import workloads as wl
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def run(cf, B, device, accumulate=False, C0=None):
+    import torch
+    plan = sc.SpMMPlan(cf, B.shape[1])
+    Bt = torch.from_numpy(B).to(device)
+    C = None if C0 is None else torch.from_numpy(np.array(C0, np.float32)).to(device)
+    out = plan.spmm(Bt, C, accumulate=accumulate)
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), plan
+
+
+@pytest.mark.parametrize("case", ["cfg1small", "ragged", "widevals"])
+@pytest.mark.parametrize("N", [1, 4, 32])
+def test_golden_cfmtx_files(cuda, case, N):
+    """.cfmtx written by the reference converter -> our kernels == C from the
+    reference's own spmm_csr_float."""
+    g = np.load(os.path.join(GOLDEN, f"spmm_{case}_n{N}.npz"))
+    a_h = sc.read_csr_from_mtx(os.path.join(GOLDEN, case + ".mtx"))
+    ip, ix, dx = a_h.arrays()
+    a = (*a_h.shape, ip, ix, dx)
+    for f in sorted(glob.glob(os.path.join(GOLDEN, f"{case}-*.cfmtx"))):
+        cf = sc.read_cfmtx(f)
+        if cf.kernel_rows > 6:
+            continue
+        C, _ = run(cf, g["B"], cuda)
+        scale = cpu.spmm_csr_abs(ip, ix, dx, g["B"])
+        assert np.all(np.abs(C.astype(np.float64) - g["C"]) <= RTOL * scale), f
+        assert_parity(C, a, g["B"])
+
+
+def test_config1(cuda):
+    a, B = wl.config1()
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 2, 4)
+    C, plan = run(cf, B, cuda)
+    assert plan.info["nnz"] == len(a[3])
+    assert_parity(C, a, B)
+
+
+@pytest.mark.parametrize("sparsity", wl.CONFIG2_SPARSITIES)
+@pytest.mark.parametrize("N", [1, 2, 4])
+def test_config2_small_b(cuda, sparsity, N):
+    a, B = wl.config2(sparsity, N)
+    h = to_csr_handle(a)
+    grid = [(m, n) for m in range(1, 7) for n in range(1, 9)] if sparsity == 0.9 else \
+        [(1, 1), (2, 4), (4, 1), (6, 8), (3, 0)]
+    for m, n in grid:
+        cf = sc.csr_to_compressed_format_converter(h, m, n)
+        C, plan = run(cf, B, cuda)
+        assert plan.info["kernel"] == 1
+        assert_parity(C, a, B)
+
+
+@pytest.mark.parametrize("shape", [(2048, 512), (512, 2048)])
+@pytest.mark.parametrize("N", [32, 64, 128])
+def test_config3_large_b(cuda, shape, N):
+    a, B = wl.config3(shape, N)
+    h = to_csr_handle(a)
+    for m in range(1, 7):
+        cf = sc.csr_to_compressed_format_converter(h, m, 1)
+        C, plan = run(cf, B, cuda)
+        assert plan.info["kernel"] == 2
+        assert_parity(C, a, B)
+
+
+def test_config4_layer_stack(cuda):
+    for name, a, B in wl.config4(128):
+        cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+        C, _ = run(cf, B, cuda)
+        assert_parity(C, a, B)
+
+
+@pytest.mark.parametrize("N", [3, 5, 8, 16, 33, 96, 200, 256])
+def test_odd_widths_and_strides(cuda, N):
+    import torch
+    a, _ = wl.config3((2048, 512), 32)
+    B = wl.dense_b(512, N, 9)
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 2)
+    C, _ = run(cf, B, cuda)
+    assert_parity(C, a, B)
+    # leading dimensions larger than N (column slices of wider buffers)
+    plan = sc.SpMMPlan(cf, N)
+    Bw = torch.zeros((512, N + 7), device=cuda)
+    Bw[:, :N] = torch.from_numpy(B).to(cuda)
+    Cw = torch.full((2048, N + 3), 7.0, device=cuda)
+    plan.spmm(Bw[:, :N], Cw[:, :N])
+    torch.cuda.synchronize()
+    assert_parity(Cw[:, :N].cpu().numpy(), a, B)
+    assert torch.all(Cw[:, N:] == 7.0)
+
+
+@pytest.mark.parametrize("N", [1, 4, 32, 128])
+def test_accumulate(cuda, N):
+    a, _ = wl.config2(0.8, 1)
+    B = wl.dense_b(512, N, 4)
+    C0 = wl.dense_b(512, N, 5)
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+    C, _ = run(cf, B, cuda, accumulate=True, C0=C0)
+    assert_parity(C, a, B, C0=C0)
+
+
+def test_spmv(cuda):
+    import torch
+    a, _ = wl.config2(0.9, 1)
+    x = wl.dense_b(512, 1, 6)[:, 0].copy()
+    m, n, ip, ix, dx = a
+    for km in (1, 4, 6):
+        cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), km, 1)
+        plan = sc.SpMMPlan(cf, 1)
+        y = plan.spmv(torch.from_numpy(x).to(cuda)).cpu().numpy()
+        ref = cpu.spmv_csr_float(ip, ix, dx, x)  # double accumulation (spmv_csr_float)
+        scale = cpu.spmm_csr_abs(ip, ix, dx, x[:, None])[:, 0]
+        assert np.all(np.abs(y.astype(np.float64) - ref) <= RTOL * scale)
+        y0 = wl.dense_b(512, 1, 8)[:, 0]
+        yt = torch.from_numpy(y0.copy()).to(cuda)
+        plan.spmv(torch.from_numpy(x).to(cuda), yt, accumulate=True)
+        assert np.all(np.abs(yt.cpu().numpy().astype(np.float64) - (ref + y0)) <= RTOL * (scale + np.abs(y0)))
+
+
+def test_panel_range_plans_tile_the_matrix(cuda):
+    import torch
+    a, B = wl.config3((2048, 512), 64)
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+    panels = (2048 + 3) // 4
+    cuts = [0, 100, 101, 333, panels]
+    Bt = torch.from_numpy(B).to(cuda)
+    C = torch.empty((2048, 64), device=cuda)
+    for p0, p1 in zip(cuts[:-1], cuts[1:]):
+        plan = sc.SpMMPlan(cf, 64, panel_range=(p0, p1))
+        assert plan.rows == min(2048, p1 * 4) - p0 * 4
+        plan.spmm(Bt, C[p0 * 4: p1 * 4])
+    torch.cuda.synchronize()
+    assert_parity(C.cpu().numpy(), a, B)
+
+
+def test_host_entry_point(cuda):
+    a, B = wl.config1()
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 2, 4)
+    plan = sc.SpMMPlan(cf, 32)
+    for _ in range(2):
+        C = plan.spmm_host(B)
+        assert_parity(C, a, B)
+
+
+def test_edge_matrices(cuda):
+    import torch
+    cases = [np.zeros((7, 5), np.float32), np.array([[0, 1.5, 0, 2]], np.float32), np.eye(9, dtype=np.float32),
+             np.ones((13, 3), np.float32)]
+    for A in cases:
+        a = wl.csr_from_dense(A)
+        for m, n in [(4, 1), (3, 2), (1, 3), (6, 0)]:
+            cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), m, n)
+            for N in (1, 2, 4, 32, 40):
+                B = wl.dense_b(A.shape[1], N, 3)
+                C, _ = run(cf, B, cuda)
+                assert_parity(C, a, B)
+    # a matrix with zero rows gives an empty plan
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(wl.csr_from_dense(np.zeros((0, 4), np.float32))), 4, 1)
+    plan = sc.SpMMPlan(cf, 32)
+    assert plan.rows == 0
+    plan.spmm(torch.zeros((4, 32), device=cuda), torch.zeros((0, 32), device=cuda))
+
+
+def test_deterministic(cuda):
+    a, B = wl.config3((512, 2048), 128)
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+    C1, _ = run(cf, B, cuda)
+    C2, _ = run(cf, B, cuda)
+    assert np.array_equal(C1, C2)
+
+
+def test_config5_full_size_properties(cuda):
+    """16384^2 at 95%: rows sampled against the oracle, linearity in B, and
+    agreement of a 2-way panel split with the single plan."""
+    import torch
+    a, B = wl.config5()
+    m = a[0]
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+    plan = sc.SpMMPlan(cf, 128)
+    Bt = torch.from_numpy(B).to(cuda)
+    C = plan.spmm(Bt)
+    rows = np.sort(np.random.default_rng(0).choice(m, 2048, replace=False))
+    assert_parity(C.cpu().numpy()[rows], a, B, rows=rows)
+    B2 = torch.from_numpy(wl.dense_b(m, 128, 99)).to(cuda)
+    lhs = plan.spmm(Bt + B2)
+    rhs = C + plan.spmm(B2)
+    scale = plan.spmm(Bt.abs() + B2.abs()) if False else None
+    assert torch.allclose(lhs, rhs, rtol=1e-4, atol=1e-4)
+    half = (m // 4) // 2
+    Cs = torch.empty_like(C)
+    for r in [(0, half), (half, m // 4)]:
+        p = sc.SpMMPlan(cf, 128, panel_range=r)
+        p.spmm(Bt, Cs[r[0] * 4: r[1] * 4])
+    torch.cuda.synchronize()
+    assert torch.allclose(Cs, C, rtol=1e-5, atol=1e-6)
