@@ -62,7 +62,7 @@ def workload(cfg: int, n_cols_b):
     if cfg == 5:
         N = n_cols_b or 128
         a, B = wl.config5(n_cols_b=N)
-        return "config5: A 16384x16384 fp32 95% sparse (half 4x1 runs), B 16384x%d" % N, [(a, B)]
+        return f"config5: A 16384x16384 fp32 95% sparse (half 4x1 runs), B 16384x{N}", [(a, B)]
     if cfg == 1:
         a, B = wl.config1()
         return "config1: A 512x512 p=0.10, B 512x32", [(a, B)]
@@ -216,6 +216,42 @@ def cpu_reference_rate(mats, seconds, threads):
     sample = (f"{nnz} nonzeros x N={N} in {dt:.2f} s: 512-row blocks of the {m}-row matrix "
               f"({len(ix)} nnz) visited in order")
     return gflops, kind, sample, dt
+
+
+def cusparse_baseline(mats, dev, flush, args):
+    """cuSPARSE CSR SpMM (through torch.sparse_csr_tensor @ dense, row-major B
+    and C) on the same inputs and with the same timing method: a reported
+    baseline, not part of the product path."""
+    import torch
+    try:
+        As, Bs = [], []
+        for a, B in mats:
+            m, n, ip, ix, dx = a
+            As.append(torch.sparse_csr_tensor(torch.from_numpy(ip.astype(np.int32)),
+                                              torch.from_numpy(ix.astype(np.int32)),
+                                              torch.from_numpy(dx.astype(np.float32)), size=(m, n)).to(dev))
+            Bs.append(torch.from_numpy(B).to(dev))
+        for _ in range(3):
+            for A, B in zip(As, Bs):
+                A @ B
+        torch.cuda.synchronize()
+        tot = 0.0
+        steps = min(args.steps, 50)
+        for _ in range(steps):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for A, B in zip(As, Bs):
+                A @ B
+            e.record()
+            e.synchronize()
+            tot += s.elapsed_time(e)
+        ms = tot / steps
+        flops = 2.0 * sum(len(a[3]) * B.shape[1] for a, B in mats)
+        return {"value": flops / (ms * 1e-3) / 1e9, "unit": "GFLOP/s", "ms_per_step": ms,
+                "how": "torch.sparse_csr_tensor @ dense (cusparseSpMM, CSR int32, row-major)"}
+    except Exception as ex:  # reported baseline only
+        return {"unavailable": str(ex)[:200]}
 
 
 # ----------------------------------------------------------- reference ---
@@ -438,6 +474,8 @@ def main():
         "clocks": clk,
         "setup_s": t_setup,
     }
+    if world == 1:
+        line["cusparse"] = cusparse_baseline(mats, dev, flush, args)
     if world == 1 and not args.no_cpu_baseline:
         g, kind, sample, dt = cpu_reference_rate(mats, args.cpu_seconds, 1)
         line["cpu_baseline"] = {"value": g, "unit": "GFLOP/s", "cores": 1, "kind": kind,

@@ -91,28 +91,65 @@ __device__ __forceinline__ void load_rec(const uint32_t *__restrict__ r, int &co
 }
 
 // ------------------------------------------------------------ wide B ------
-// One warp walks the entries of an item in order; lane l owns C columns
-// [col0, col0+VEC) with col0 = slice*32*VEC + l*VEC.  Per entry: one
-// warp-uniform record load, one coalesced VEC-wide load of the B row, and
-// P*VEC FMAs into the mask's rows.
+// One warp walks the entries of an item; lane l owns C columns
+// [col0, col0+VEC) with col0 = slice*32*VEC + l*VEC.
+//
+// Latency structure: the records of an item (<= 32 entries) are fetched
+// lane-parallel in one coalesced load (lane e holds entry e's record), one
+// item ahead of use, so the record stream's DRAM latency overlaps the
+// previous item's B loads.  Entries are then broadcast with warp shuffles and
+// their B rows fetched U at a time (U independent 32*VEC-wide loads in
+// flight per warp) before the P*VEC FMAs per entry.
+
+// Record words of one entry of an item, held by the lane of that entry.
+struct ItemRecs {
+  uint32_t w[8];
+};
+
+// Lane-parallel load of an item's records (stride S words, len entries).
+__device__ __forceinline__ void load_item_recs(const uint32_t *__restrict__ recs, int2 item, int lane,
+                                               ItemRecs &r) {
+  const int mask = item.y & 0xffff;
+  const int len = item.y >> 16;
+  const int P = __popc(mask);
+  const uint32_t *base = recs + (uint32_t)item.x;
+  if (lane < len) {
+    if (P == 1) {
+      uint2 t = __ldg(reinterpret_cast<const uint2 *>(base) + lane);
+      r.w[0] = t.x; r.w[1] = t.y;
+    } else if (P <= 3) {
+      uint4 t = __ldg(reinterpret_cast<const uint4 *>(base) + lane);
+      r.w[0] = t.x; r.w[1] = t.y; r.w[2] = t.z; r.w[3] = t.w;
+    } else {
+      uint4 t0 = __ldg(reinterpret_cast<const uint4 *>(base) + 2 * lane);
+      uint4 t1 = __ldg(reinterpret_cast<const uint4 *>(base) + 2 * lane + 1);
+      r.w[0] = t0.x; r.w[1] = t0.y; r.w[2] = t0.z; r.w[3] = t0.w;
+      r.w[4] = t1.x; r.w[5] = t1.y; r.w[6] = t1.z; r.w[7] = t1.w;
+    }
+  }
+}
+
 template <int KM, int MASK, int VEC>
-__device__ __forceinline__ void seg_wide(const uint32_t *__restrict__ rec, int len,
-                                         const float *__restrict__ Bcol, int64_t ldb, bool active,
-                                         float (&acc)[KM][VEC]) {
+__device__ __forceinline__ void seg_wide(const ItemRecs &r, int len, const float *__restrict__ Bcol,
+                                         int64_t ldb, bool active, float (&acc)[KM][VEC]) {
   constexpr int P = popc_c(MASK);
-  constexpr int S = rec_stride(P);
-  constexpr int U = 4;
-  int e = 0;
-  for (; e + U <= len; e += U) {
+  constexpr int U = P <= 2 ? 8 : 4;
+  for (int e0 = 0; e0 < len; e0 += U) {
     int col[U];
     float v[U][P];
     float b[U][VEC];
 #pragma unroll
-    for (int u = 0; u < U; ++u) load_rec<P>(rec + (e + u) * S, col[u], v[u]);
+    for (int u = 0; u < U; ++u) {
+      const int e = min(e0 + u, len - 1);
+      col[u] = (int)__shfl_sync(0xffffffffu, r.w[0], e);
+#pragma unroll
+      for (int p = 0; p < P; ++p) v[u][p] = __uint_as_float(__shfl_sync(0xffffffffu, r.w[1 + p], e));
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      if (active) load_vec<VEC>(Bcol + (int64_t)col[u] * ldb, b[u]);
-      else {
+      if (active && e0 + u < len) {
+        load_vec<VEC>(Bcol + (int64_t)col[u] * ldb, b[u]);
+      } else {
 #pragma unroll
         for (int q = 0; q < VEC; ++q) b[u][q] = 0.f;
       }
@@ -122,40 +159,26 @@ __device__ __forceinline__ void seg_wide(const uint32_t *__restrict__ rec, int l
 #pragma unroll
       for (int p = 0; p < P; ++p)
 #pragma unroll
-        for (int q = 0; q < VEC; ++q) acc[nth_row(MASK, p)][q] = fmaf(v[u][p], b[u][q], acc[nth_row(MASK, p)][q]);
-  }
-  for (; e < len; ++e) {
-    int col;
-    float v[P];
-    float b[VEC];
-    load_rec<P>(rec + e * S, col, v);
-    if (active) load_vec<VEC>(Bcol + (int64_t)col * ldb, b);
-    else {
-#pragma unroll
-      for (int q = 0; q < VEC; ++q) b[q] = 0.f;
-    }
-#pragma unroll
-    for (int p = 0; p < P; ++p)
-#pragma unroll
-      for (int q = 0; q < VEC; ++q) acc[nth_row(MASK, p)][q] = fmaf(v[p], b[q], acc[nth_row(MASK, p)][q]);
+        for (int q = 0; q < VEC; ++q)
+          acc[nth_row(MASK, p)][q] = fmaf(v[u][p], b[u][q], acc[nth_row(MASK, p)][q]);
   }
 }
 
 template <int KM, int VEC, int LO, int HI>
-__device__ __forceinline__ void dispatch_wide(int mask, const uint32_t *__restrict__ rec, int len,
+__device__ __forceinline__ void dispatch_wide(int mask, const ItemRecs &r, int len,
                                               const float *__restrict__ Bcol, int64_t ldb, bool active,
                                               float (&acc)[KM][VEC]) {
   if constexpr (HI - LO == 1) {
-    seg_wide<KM, LO, VEC>(rec, len, Bcol, ldb, active, acc);
+    seg_wide<KM, LO, VEC>(r, len, Bcol, ldb, active, acc);
   } else {
     constexpr int MID = (LO + HI) / 2;
-    if (mask < MID) dispatch_wide<KM, VEC, LO, MID>(mask, rec, len, Bcol, ldb, active, acc);
-    else dispatch_wide<KM, VEC, MID, HI>(mask, rec, len, Bcol, ldb, active, acc);
+    if (mask < MID) dispatch_wide<KM, VEC, LO, MID>(mask, r, len, Bcol, ldb, active, acc);
+    else dispatch_wide<KM, VEC, MID, HI>(mask, r, len, Bcol, ldb, active, acc);
   }
 }
 
 template <int KM, int VEC>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
 spmm_wide_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ items,
                  const int32_t *__restrict__ item_ptr, const int32_t *__restrict__ order,
                  const float *__restrict__ B, int64_t ldb, float *__restrict__ C, int64_t ldc,
@@ -176,11 +199,21 @@ spmm_wide_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ ite
     for (int q = 0; q < VEC; ++q) acc[k][q] = 0.f;
 
   const int it0 = item_ptr[panel], it1 = item_ptr[panel + 1];
-  for (int it = it0 + warp; it < it1; it += nw) {
-    const int2 item = __ldg(items + it);
-    const int mask = item.y & 0xffff;
-    const int len = item.y >> 16;
-    dispatch_wide<KM, VEC, 1, (1 << KM)>(mask, recs + (uint32_t)item.x, len, Bcol, ldb, active, acc);
+  int it = it0 + warp;
+  ItemRecs nxt;
+  int2 nitem = make_int2(0, 0);
+  if (it < it1) {
+    nitem = __ldg(items + it);
+    load_item_recs(recs, nitem, lane, nxt);
+  }
+  for (; it < it1; it += nw) {
+    const ItemRecs cur = nxt;
+    const int2 item = nitem;
+    if (it + nw < it1) {  // prefetch the next item's records
+      nitem = __ldg(items + it + nw);
+      load_item_recs(recs, nitem, lane, nxt);
+    }
+    dispatch_wide<KM, VEC, 1, (1 << KM)>(item.y & 0xffff, cur, item.y >> 16, Bcol, ldb, active, acc);
   }
 
   if (nw > 1) {

@@ -245,9 +245,9 @@ bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 
 void launch(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int accumulate,
             cudaStream_t stream) {
-  require(B != nullptr && C != nullptr, SC_ERR_ARG, "null B or C");
   require(ldb >= p->n && ldc >= p->n, SC_ERR_ARG, "leading dimension smaller than n_cols_b");
-  if (p->panels == 0) return;
+  if (p->panels == 0 || p->rows == 0) return;  // nothing to write (C may be an empty buffer)
+  require(B != nullptr && C != nullptr, SC_ERR_ARG, "null B or C");
   DeviceGuard dg(p->device);
   const int threads = 32 * p->warps;
   const int nb = (int)p->n;
