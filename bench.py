@@ -310,35 +310,65 @@ def main():
 
     # ---- setup: this rank's row blocks, coarsening, plans (untimed)
     t_setup = time.perf_counter()
-    jobs = []  # (plan, B device, C block view, rows, global row offset, nnz)
-    total_nnz = 0
-    for a, B in mats:
-        m = a[0]
-        total_nnz += len(a[3])
-        cuts = balanced_panel_cuts(a[2], m, km, world)
-        p0, p1 = cuts[rank], cuts[rank + 1]
-        r0, r1 = min(p0 * km, m), min(p1 * km, m)
-        blk = row_slice(a, r0, r1)
-        cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*blk), km, kn)
-        plan = sc.SpMMPlan(cf, N, device=local)
-        max_rows = max(min(cuts[r + 1] * km, m) - min(cuts[r] * km, m) for r in range(world))
-        jobs.append({"plan": plan, "B": torch.from_numpy(B).to(dev), "rows": r1 - r0, "max_rows": max_rows,
-                     "m": m, "nnz_local": len(blk[3]), "Bhost": B, "cuts": cuts})
+    layers = args.config == 4  # independent matrices: shard whole matrices, no collective
+    jobs = []
+    total_nnz = sum(len(a[3]) for a, _ in mats)
+    if layers:
+        # greedy LPT assignment of whole matrices to ranks by nonzeros
+        load = [0] * world
+        owner = []
+        for i in sorted(range(len(mats)), key=lambda i: -len(mats[i][0][3])):
+            r = min(range(world), key=lambda r: load[r])
+            load[r] += len(mats[i][0][3])
+            owner.append((i, r))
+        mine = sorted(i for i, r in owner if r == rank)
+        for i in mine:
+            a, B = mats[i]
+            cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*a), km, kn)
+            plan = sc.SpMMPlan(cf, N, device=local)
+            jobs.append({"plan": plan, "B": torch.from_numpy(B).to(dev), "rows": a[0], "max_rows": a[0],
+                         "m": a[0], "nnz_local": len(a[3]), "Bhost": B, "cuts": None, "K": a[1],
+                         "C": torch.empty((a[0], N), device=dev)})
+    else:
+        for a, B in mats:
+            m = a[0]
+            cuts = balanced_panel_cuts(a[2], m, km, world)
+            p0, p1 = cuts[rank], cuts[rank + 1]
+            r0, r1 = min(p0 * km, m), min(p1 * km, m)
+            blk = row_slice(a, r0, r1)
+            cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*blk), km, kn)
+            plan = sc.SpMMPlan(cf, N, device=local)
+            max_rows = max(min(cuts[r + 1] * km, m) - min(cuts[r] * km, m) for r in range(world))
+            j = {"plan": plan, "B": torch.from_numpy(B).to(dev), "rows": r1 - r0, "max_rows": max_rows,
+                 "m": m, "nnz_local": len(blk[3]), "Bhost": B, "cuts": cuts, "K": a[1]}
+            j["gather"] = torch.empty((world, max_rows, N), device=dev)
+            j["C"] = j["gather"][rank, : j["rows"]] if world > 1 else torch.empty((j["rows"], N), device=dev)
+            jobs.append(j)
+    batch = None
+    if len(jobs) > 1 and jobs[0]["plan"].info["kernel"] == 2:
+        batch = sc.SpMMBatch([j["plan"] for j in jobs])
+        batch.bind([j["B"] for j in jobs], [j["C"] for j in jobs])
     t_setup = time.perf_counter() - t_setup
-    for j in jobs:
-        j["gather"] = torch.empty((world, j["max_rows"], N), device=dev)
-        j["C"] = j["gather"][rank, : j["rows"]] if world > 1 else torch.empty((j["rows"], N), device=dev)
+
+    def launch_all(stream):
+        if batch is not None:
+            batch.spmm(stream=stream)  # every local matrix in one kernel launch
+        else:
+            for j in jobs:
+                j["plan"].spmm(j["B"], j["C"], stream=stream)
+
+    def gather_all():
+        if world > 1 and not layers:
+            for j in jobs:
+                # in place: this rank's block already sits at its slot
+                dist.all_gather_into_tensor(j["gather"], j["gather"][rank])
 
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def step():
-        for j in jobs:
-            j["plan"].spmm(j["B"], j["C"], stream=stream)
-        if world > 1:
-            for j in jobs:
-                # in place: this rank's block already sits at its slot
-                dist.all_gather_into_tensor(j["gather"], j["gather"][rank])
+        launch_all(stream)
+        gather_all()
 
     kernel_events = []
 
@@ -358,12 +388,9 @@ def main():
             flush.zero_()
             starts[i].record(stream)
             kstarts[i].record(stream)
-            for j in jobs:
-                j["plan"].spmm(j["B"], j["C"], stream=stream)
+            launch_all(stream)
             kends[i].record(stream)
-            if world > 1:
-                for j in jobs:
-                    dist.all_gather_into_tensor(j["gather"], j["gather"][rank])
+            gather_all()
             ends[i].record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -395,11 +422,12 @@ def main():
             def e2e_step():
                 for j, hB in zip(jobs, hBs):
                     j["B"].copy_(hB, non_blocking=True)
-                    j["plan"].spmm(j["B"], j["C"], stream=stream)
-                if world > 1:
-                    for j in jobs:
-                        dist.all_gather_into_tensor(j["gather"], j["gather"][rank])
-                if rank == 0:
+                launch_all(stream)
+                gather_all()
+                if layers:
+                    for j, hC in zip(jobs, hCs):
+                        hC.copy_(j["C"], non_blocking=True)
+                elif rank == 0:
                     for j, hC in zip(jobs, hCs):
                         for r in range(world):
                             a0 = min(j["cuts"][r] * km, j["m"])
@@ -417,7 +445,7 @@ def main():
                 e2e_step()
             e2e_s = (time.perf_counter() - t0) / e2e_steps
             h2d = sum(j["Bhost"].nbytes for j in jobs)
-            d2h = sum(j["m"] * N * 4 for j in jobs) if rank == 0 else 0
+            d2h = sum(j["m"] * N * 4 for j in jobs) if (rank == 0 or layers) else 0
 
     # ---- reduce over ranks (max time)
     t = torch.tensor([step_ms, kern_ms, e2e_s], dtype=torch.float64, device=dev)
@@ -435,13 +463,8 @@ def main():
         return
 
     # ---- roofline of the dominant kernel (the SpMM launch of this rank)
-    K = mats[0][0][1]
-    M = mats[0][0][0]
-    if world == 1:
-        alg_bytes = sum(4.0 * len(a[3]) + 4.0 * a[1] * N + 4.0 * a[0] * N for a, _ in mats)
-    else:
-        j = jobs[0]
-        alg_bytes = 4.0 * j["nnz_local"] + 4.0 * K * N + 4.0 * j["rows"] * N
+    # this rank's launch(es): values + B read once + C written once, per matrix
+    alg_bytes = sum(4.0 * j["nnz_local"] + 4.0 * j["K"] * N + 4.0 * j["rows"] * N for j in jobs)
     peak, peak_kind = measured_peak_hbm()
     achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
     props = torch.cuda.get_device_properties(dev)
@@ -457,7 +480,10 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
         "config": {"workload": name, "coarsening": [km, kn], "n_cols_b": N, "nnz": total_nnz,
-                   "parallelism": f"row-partition x{world} + NCCL all-gather of C" if world > 1 else "1 GPU",
+                   "parallelism": ("1 GPU" if world == 1 else
+                                   f"whole matrices sharded over {world} GPUs (LPT by nnz), no collective"
+                                   if layers else f"row-partition x{world} + NCCL all-gather of C"),
+                   "launches_per_step": 1 if batch is not None else len(jobs),
                    "l2": "flushed before every timed step (256 MiB write, outside the events)",
                    "plan": {k: info[k] for k in ("entries", "items", "kernel", "warps_per_panel",
                                                  "device_bytes")}},
@@ -470,7 +496,7 @@ def main():
                      "fp32_frac": local_flops / (kern_ms * 1e-3) / 1e12 / fp32_peak},
         "e2e": {"value": e2e_value, "unit": "GFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_s * 1e3},
-        "gpu_launches": args.steps * len(jobs),
+        "gpu_launches": args.steps * (1 if batch is not None else len(jobs)),
         "clocks": clk,
         "setup_s": t_setup,
     }

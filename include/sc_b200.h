@@ -146,6 +146,26 @@ int sc_spmv(sc_plan *p, const float *dx, float *dy, int32_t accumulate, void *st
 int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream);
 void sc_plan_free(sc_plan *p);
 
+/* ------------------------------------------------------------- batches ---- */
+
+typedef struct sc_batch sc_batch; /* several plans executed by one kernel launch */
+
+/* Groups plans that share device, kernel_m and n_cols_b (wide-B widths, i.e.
+ * n_cols_b not in {1,2,4}) so that all their row panels run in ONE launch,
+ * heaviest panels first -- e.g. the 96 weight matrices of a transformer layer
+ * stack.  Replaces one reference launch per matrix
+ * (example_cuda/spmm_demo_gpu_utils.h:1705-1712).  The plans must outlive
+ * the batch. */
+int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out);
+/* Binds the operands of every plan (arrays of `count` device pointers and
+ * leading dimensions, same meaning as for sc_spmm).  Synchronous upload;
+ * re-bind whenever a buffer changes. */
+int sc_batch_bind(sc_batch *b, const float *const *dB, const int64_t *ldb, float *const *dC,
+                  const int64_t *ldc);
+/* C_i = A_i*B_i (or +=) for all plans of the batch, one kernel launch. */
+int sc_batch_spmm(sc_batch *b, int32_t accumulate, void *stream);
+void sc_batch_free(sc_batch *b);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,7 +31,7 @@ from typing import Dict, Optional, Tuple
 import numpy as np
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "libsc_b200.so")
+LIB_PATH = os.environ.get("SC_LIB", os.path.join(_PKG, "libsc_b200.so"))
 
 SC_OK = 0
 SC_ERR_ARG = 1
@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "sc_companion_mtx_path",
     "sc_plan_create", "sc_plan_create_panels", "sc_plan_get_info", "sc_spmm", "sc_spmv",
     "sc_spmm_host", "sc_plan_free",
+    "sc_batch_create", "sc_batch_bind", "sc_batch_spmm", "sc_batch_free",
 )
 
 
@@ -107,6 +108,10 @@ def lib() -> ctypes.CDLL:
         "sc_spmv": ([vp, vp, vp, i32, vp], ctypes.c_int),
         "sc_spmm_host": ([vp, vp, vp, vp], ctypes.c_int),
         "sc_plan_free": ([vp], None),
+        "sc_batch_create": ([vp, i32, P(vp)], ctypes.c_int),
+        "sc_batch_bind": ([vp, vp, vp, vp, vp], ctypes.c_int),
+        "sc_batch_spmm": ([vp, i32, vp], ctypes.c_int),
+        "sc_batch_free": ([vp], None),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -384,4 +389,46 @@ class SpMMPlan:
     def __del__(self):
         if getattr(self, "_h", None) and self._h.value and _lib is not None:
             _lib.sc_plan_free(self._h)
+            self._h = ctypes.c_void_p()
+
+
+class SpMMBatch:
+    """Several plans (same device, kernel_m and B width) computed by ONE
+    kernel launch: ``bind(Bs, Cs)`` once, then ``spmm()`` per step."""
+
+    def __init__(self, plans):
+        self.plans = list(plans)
+        arr = (ctypes.c_void_p * len(self.plans))(*[p._h.value for p in self.plans])
+        h = ctypes.c_void_p()
+        _check(lib().sc_batch_create(arr, len(self.plans), ctypes.byref(h)))
+        self._h = h
+        self._bound = None
+
+    def bind(self, Bs, Cs):
+        torch = _torch()
+        n = len(self.plans)
+        if len(Bs) != n or len(Cs) != n:
+            raise ScError(SC_ERR_ARG, f"need {n} B and {n} C tensors")
+        for p, B, C in zip(self.plans, Bs, Cs):
+            if B.dtype != torch.float32 or C.dtype != torch.float32 or B.stride(1) != 1 or C.stride(1) != 1:
+                raise ScError(SC_ERR_ARG, "B and C must be float32 with unit column stride")
+            if tuple(B.shape) != (p.cols, p.n) or tuple(C.shape) != (p.rows, p.n):
+                raise ScError(SC_ERR_ARG, "operand shapes do not match the plans")
+        bp = (ctypes.c_void_p * n)(*[B.data_ptr() for B in Bs])
+        cp = (ctypes.c_void_p * n)(*[C.data_ptr() for C in Cs])
+        lb = (ctypes.c_int64 * n)(*[B.stride(0) for B in Bs])
+        lc = (ctypes.c_int64 * n)(*[C.stride(0) for C in Cs])
+        _check(lib().sc_batch_bind(self._h, bp, lb, cp, lc))
+        self._bound = (list(Bs), list(Cs))  # keep the buffers alive
+
+    def spmm(self, accumulate: bool = False, stream=None):
+        torch = _torch()
+        dev = self.plans[0].device
+        s = stream if stream is not None else torch.cuda.current_stream(dev)
+        _check(lib().sc_batch_spmm(self._h, 1 if accumulate else 0, ctypes.c_void_p(s.cuda_stream)))
+        return self._bound[1] if self._bound else None
+
+    def __del__(self):
+        if getattr(self, "_h", None) and self._h.value and _lib is not None:
+            _lib.sc_batch_free(self._h)
             self._h = ctypes.c_void_p()

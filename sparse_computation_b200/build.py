@@ -16,8 +16,10 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
-BUILD = os.path.join(ROOT, "_build")
-LIB = os.path.join(PKG, "libsc_b200.so")
+BUILD = os.environ.get("SC_BUILD_DIR", os.path.join(ROOT, "_build"))
+LIB = os.environ.get("SC_LIB", os.path.join(PKG, "libsc_b200.so"))
+# Extra nvcc flags (e.g. tuning macros such as -DSC_WIDE_MINB=2) for experiments.
+EXTRA_NVCC = os.environ.get("SC_NVCC_FLAGS", "").split()
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -61,7 +63,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
         if force or not _newer(o, [s] + headers):
             jobs.append([NVCC, *ARCH, "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
                          "-Xptxas", "-v" if verbose else "-O3",
-                         *extra, "-I", INCLUDE, "-I", CSRC, "-c", s, "-o", o])
+                         *extra, *EXTRA_NVCC, "-I", INCLUDE, "-I", CSRC, "-c", s, "-o", o])
     with ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
         for out in ex.map(_run, jobs):
             if verbose and out:

@@ -9,11 +9,18 @@
 #define SC_CAT2(a, b) a##b
 #define SC_CAT(a, b) SC_CAT2(a, b)
 
-sc::WideFn SC_CAT(sc_wide_kernel_km, SC_KM)(int vec) {
+sc::WideFn SC_CAT(sc_wide_kernel_km, SC_KM)(int vec, bool batch) {
+  if (batch) {
+    switch (vec) {
+      case 1: return sc::spmm_wide_kernel<SC_KM, 1, true>;
+      case 2: return sc::spmm_wide_kernel<SC_KM, 2, true>;
+      default: return sc::spmm_wide_kernel<SC_KM, 4, true>;
+    }
+  }
   switch (vec) {
-    case 1: return sc::spmm_wide_kernel<SC_KM, 1>;
-    case 2: return sc::spmm_wide_kernel<SC_KM, 2>;
-    default: return sc::spmm_wide_kernel<SC_KM, 4>;
+    case 1: return sc::spmm_wide_kernel<SC_KM, 1, false>;
+    case 2: return sc::spmm_wide_kernel<SC_KM, 2, false>;
+    default: return sc::spmm_wide_kernel<SC_KM, 4, false>;
   }
 }
 

@@ -94,61 +94,89 @@ __device__ __forceinline__ void load_rec(const uint32_t *__restrict__ r, int &co
 // One warp walks the entries of an item; lane l owns C columns
 // [col0, col0+VEC) with col0 = slice*32*VEC + l*VEC.
 //
-// Latency structure: the records of an item (<= 32 entries) are fetched
-// lane-parallel in one coalesced load (lane e holds entry e's record), one
-// item ahead of use, so the record stream's DRAM latency overlaps the
-// previous item's B loads.  Entries are then broadcast with warp shuffles and
-// their B rows fetched U at a time (U independent 32*VEC-wide loads in
-// flight per warp) before the P*VEC FMAs per entry.
+// Per warp, the records of the next item are copied global -> shared with
+// cp.async (16 B per lane, bypassing L1) while the current item is
+// processed, so the record stream's DRAM latency overlaps the B loads.  Each
+// entry's record is then read with one broadcast shared load, its B row
+// address formed with one 32x32->64 multiply-add, and U entries' B rows are
+// loaded (U independent 32*VEC-wide loads in flight) before the P*VEC FMAs.
 
-// Record words of one entry of an item, held by the lane of that entry.
-struct ItemRecs {
-  uint32_t w[8];
+// Operands of one matrix for the wide kernel.
+struct WideArgs {
+  const uint32_t *recs;
+  const int2 *items;
+  const int32_t *item_ptr;
+  const float *B;
+  float *C;
+  int64_t ldc;
+  int64_t rows;
+  uint32_t ldb_bytes;  // row pitch of B in bytes (< 4 GiB)
+  int n_cols;
 };
 
-// Lane-parallel load of an item's records (stride S words, len entries).
-__device__ __forceinline__ void load_item_recs(const uint32_t *__restrict__ recs, int2 item, int lane,
-                                               ItemRecs &r) {
-  const int mask = item.y & 0xffff;
+#ifndef SC_WIDE_U
+#define SC_WIDE_U 8
+#endif
+#ifndef SC_WIDE_MINB
+#define SC_WIDE_MINB 3
+#endif
+constexpr int kRecBufWords = kItemEntries * 8;  // one item of the widest stride
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+
+// Warp-cooperative copy of an item's records (16-byte chunks) into `dst`.
+__device__ __forceinline__ void copy_item_recs(uint32_t *dst, const uint32_t *__restrict__ recs, int2 item,
+                                               int lane) {
   const int len = item.y >> 16;
-  const int P = __popc(mask);
-  const uint32_t *base = recs + (uint32_t)item.x;
-  if (lane < len) {
-    if (P == 1) {
-      uint2 t = __ldg(reinterpret_cast<const uint2 *>(base) + lane);
-      r.w[0] = t.x; r.w[1] = t.y;
-    } else if (P <= 3) {
-      uint4 t = __ldg(reinterpret_cast<const uint4 *>(base) + lane);
-      r.w[0] = t.x; r.w[1] = t.y; r.w[2] = t.z; r.w[3] = t.w;
-    } else {
-      uint4 t0 = __ldg(reinterpret_cast<const uint4 *>(base) + 2 * lane);
-      uint4 t1 = __ldg(reinterpret_cast<const uint4 *>(base) + 2 * lane + 1);
-      r.w[0] = t0.x; r.w[1] = t0.y; r.w[2] = t0.z; r.w[3] = t0.w;
-      r.w[4] = t1.x; r.w[5] = t1.y; r.w[6] = t1.z; r.w[7] = t1.w;
-    }
+  const int P = __popc(item.y & 0xffff);
+  const int S = P == 1 ? 2 : (P <= 3 ? 4 : 8);
+  const int chunks = (len * S + 3) >> 2;
+  const uint4 *src = reinterpret_cast<const uint4 *>(recs + (uint32_t)item.x);
+  for (int c = lane; c < chunks; c += 32) cp_async16(reinterpret_cast<uint4 *>(dst) + c, src + c);
+}
+
+template <int P>
+__device__ __forceinline__ void lds_rec(const uint32_t *r, uint32_t &col, float (&v)[P]) {
+  constexpr int S = rec_stride(P);
+  if constexpr (S == 2) {
+    const uint2 t = *reinterpret_cast<const uint2 *>(r);
+    col = t.x; v[0] = __uint_as_float(t.y);
+  } else if constexpr (S == 4) {
+    const uint4 t = *reinterpret_cast<const uint4 *>(r);
+    col = t.x;
+    const uint32_t w[3] = {t.y, t.z, t.w};
+#pragma unroll
+    for (int p = 0; p < P; ++p) v[p] = __uint_as_float(w[p]);
+  } else {
+    const uint4 a = *reinterpret_cast<const uint4 *>(r);
+    const uint4 b = *(reinterpret_cast<const uint4 *>(r) + 1);
+    col = a.x;
+    const uint32_t w[7] = {a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int p = 0; p < P; ++p) v[p] = __uint_as_float(w[p]);
   }
 }
 
 template <int KM, int MASK, int VEC>
-__device__ __forceinline__ void seg_wide(const ItemRecs &r, int len, const float *__restrict__ Bcol,
-                                         int64_t ldb, bool active, float (&acc)[KM][VEC]) {
+__device__ __forceinline__ void seg_wide(const uint32_t *rbuf, int len, const char *__restrict__ Bcol,
+                                         uint32_t ldb_bytes, bool active, float (&acc)[KM][VEC]) {
   constexpr int P = popc_c(MASK);
-  constexpr int U = P <= 2 ? 8 : 4;
+  constexpr int S = rec_stride(P);
+  constexpr int U = P <= 2 ? SC_WIDE_U : 4;
   for (int e0 = 0; e0 < len; e0 += U) {
-    int col[U];
     float v[U][P];
     float b[U][VEC];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int e = min(e0 + u, len - 1);
-      col[u] = (int)__shfl_sync(0xffffffffu, r.w[0], e);
-#pragma unroll
-      for (int p = 0; p < P; ++p) v[u][p] = __uint_as_float(__shfl_sync(0xffffffffu, r.w[1 + p], e));
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
+      uint32_t col;
+      lds_rec<P>(rbuf + min(e0 + u, len - 1) * S, col, v[u]);
       if (active && e0 + u < len) {
-        load_vec<VEC>(Bcol + (int64_t)col[u] * ldb, b[u]);
+        load_vec<VEC>(reinterpret_cast<const float *>(Bcol + (uint64_t)col * ldb_bytes), b[u]);
       } else {
 #pragma unroll
         for (int q = 0; q < VEC; ++q) b[u][q] = 0.f;
@@ -165,32 +193,49 @@ __device__ __forceinline__ void seg_wide(const ItemRecs &r, int len, const float
 }
 
 template <int KM, int VEC, int LO, int HI>
-__device__ __forceinline__ void dispatch_wide(int mask, const ItemRecs &r, int len,
-                                              const float *__restrict__ Bcol, int64_t ldb, bool active,
+__device__ __forceinline__ void dispatch_wide(int mask, const uint32_t *rbuf, int len,
+                                              const char *__restrict__ Bcol, uint32_t ldb_bytes, bool active,
                                               float (&acc)[KM][VEC]) {
   if constexpr (HI - LO == 1) {
-    seg_wide<KM, LO, VEC>(r, len, Bcol, ldb, active, acc);
+    seg_wide<KM, LO, VEC>(rbuf, len, Bcol, ldb_bytes, active, acc);
   } else {
     constexpr int MID = (LO + HI) / 2;
-    if (mask < MID) dispatch_wide<KM, VEC, LO, MID>(mask, r, len, Bcol, ldb, active, acc);
-    else dispatch_wide<KM, VEC, MID, HI>(mask, r, len, Bcol, ldb, active, acc);
+    if (mask < MID) dispatch_wide<KM, VEC, LO, MID>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+    else dispatch_wide<KM, VEC, MID, HI>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
   }
 }
 
-template <int KM, int VEC>
-__global__ void __launch_bounds__(256, 2)
-spmm_wide_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ items,
-                 const int32_t *__restrict__ item_ptr, const int32_t *__restrict__ order,
-                 const float *__restrict__ B, int64_t ldb, float *__restrict__ C, int64_t ldc,
-                 int64_t rows, int n_cols, int accumulate) {
-  extern __shared__ float red[];  // [warps-1][KM][32*VEC]
+// Dynamic shared memory: max(2 record buffers per warp, the cross-warp
+// reduction area (warps-1) x KM x 32*VEC floats).
+__host__ __device__ constexpr size_t wide_smem_bytes(int warps, int km, int vec) {
+  return (size_t)4 * ((size_t)warps * 2 * kRecBufWords > (size_t)(warps - 1) * km * 32 * vec
+                          ? (size_t)warps * 2 * kRecBufWords
+                          : (size_t)(warps - 1) * km * 32 * vec);
+}
+
+// BATCH == false: CTA b computes panel order[b] of `one`.
+// BATCH == true : CTA b computes panel order2[b].y of matrix many[order2[b].x]
+//                 (a whole set of matrices -- e.g. a layer stack -- in one launch).
+template <int KM, int VEC, bool BATCH>
+__global__ void __launch_bounds__(256, SC_WIDE_MINB)
+spmm_wide_kernel(WideArgs one, const WideArgs *__restrict__ many, const int32_t *__restrict__ order,
+                 int accumulate) {
+  extern __shared__ __align__(16) uint32_t smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nw = blockDim.x >> 5;
-  const int panel = order[blockIdx.x];
+  int panel;
+  if constexpr (BATCH) {
+    const int2 o = reinterpret_cast<const int2 *>(order)[blockIdx.x];
+    one = many[o.x];
+    panel = o.y;
+  } else {
+    panel = order[blockIdx.x];
+  }
   const int col0 = blockIdx.y * 32 * VEC + lane * VEC;
-  const bool active = col0 < n_cols;
-  const float *Bcol = B + col0;
+  const bool active = col0 < one.n_cols;
+  const char *Bcol = reinterpret_cast<const char *>(one.B + col0);
+  uint32_t *rbuf = smem + warp * 2 * kRecBufWords;
 
   float acc[KM][VEC];
 #pragma unroll
@@ -198,25 +243,33 @@ spmm_wide_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ ite
 #pragma unroll
     for (int q = 0; q < VEC; ++q) acc[k][q] = 0.f;
 
-  const int it0 = item_ptr[panel], it1 = item_ptr[panel + 1];
+  const int it0 = one.item_ptr[panel], it1 = one.item_ptr[panel + 1];
   int it = it0 + warp;
-  ItemRecs nxt;
   int2 nitem = make_int2(0, 0);
   if (it < it1) {
-    nitem = __ldg(items + it);
-    load_item_recs(recs, nitem, lane, nxt);
+    nitem = __ldg(one.items + it);
+    copy_item_recs(rbuf, one.recs, nitem, lane);
   }
+  cp_async_commit();
+  int buf = 0;
   for (; it < it1; it += nw) {
-    const ItemRecs cur = nxt;
     const int2 item = nitem;
-    if (it + nw < it1) {  // prefetch the next item's records
-      nitem = __ldg(items + it + nw);
-      load_item_recs(recs, nitem, lane, nxt);
+    if (it + nw < it1) {  // next item's records into the other buffer
+      nitem = __ldg(one.items + it + nw);
+      copy_item_recs(rbuf + (buf ^ 1) * kRecBufWords, one.recs, nitem, lane);
     }
-    dispatch_wide<KM, VEC, 1, (1 << KM)>(item.y & 0xffff, cur, item.y >> 16, Bcol, ldb, active, acc);
+    cp_async_commit();
+    cp_async_wait_1();
+    __syncwarp();
+    dispatch_wide<KM, VEC, 1, (1 << KM)>(item.y & 0xffff, rbuf + buf * kRecBufWords, item.y >> 16, Bcol,
+                                         one.ldb_bytes, active, acc);
+    __syncwarp();
+    buf ^= 1;
   }
 
   if (nw > 1) {
+    float *red = reinterpret_cast<float *>(smem);
+    __syncthreads();  // record buffers are reused as the reduction area
     if (warp > 0) {
 #pragma unroll
       for (int k = 0; k < KM; ++k)
@@ -235,8 +288,8 @@ spmm_wide_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ ite
 #pragma unroll
   for (int k = 0; k < KM; ++k) {
     const int64_t row = (int64_t)panel * KM + k;
-    if (row >= rows) break;
-    float *c = C + row * ldc + col0;
+    if (row >= one.rows) break;
+    float *c = one.C + row * one.ldc + col0;
     if constexpr (VEC == 1) {
       c[0] = accumulate ? c[0] + acc[k][0] : acc[k][0];
     } else if constexpr (VEC == 2) {
@@ -383,20 +436,19 @@ spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ i
   }
 }
 
-using WideFn = void (*)(const uint32_t *, const int2 *, const int32_t *, const int32_t *, const float *,
-                        int64_t, float *, int64_t, int64_t, int, int);
+using WideFn = void (*)(WideArgs, const WideArgs *, const int32_t *, int);
 using NarrowFn = void (*)(const uint32_t *, const int2 *, const int32_t *, const int32_t *, const float *,
                           int64_t, float *, int64_t, int64_t, int);
 
 }  // namespace sc
 
 // Per-kernel_m kernel tables, defined in sc_inst.cu (one object per kernel_m).
-sc::WideFn sc_wide_kernel_km1(int vec);
-sc::WideFn sc_wide_kernel_km2(int vec);
-sc::WideFn sc_wide_kernel_km3(int vec);
-sc::WideFn sc_wide_kernel_km4(int vec);
-sc::WideFn sc_wide_kernel_km5(int vec);
-sc::WideFn sc_wide_kernel_km6(int vec);
+sc::WideFn sc_wide_kernel_km1(int vec, bool batch);
+sc::WideFn sc_wide_kernel_km2(int vec, bool batch);
+sc::WideFn sc_wide_kernel_km3(int vec, bool batch);
+sc::WideFn sc_wide_kernel_km4(int vec, bool batch);
+sc::WideFn sc_wide_kernel_km5(int vec, bool batch);
+sc::WideFn sc_wide_kernel_km6(int vec, bool batch);
 sc::NarrowFn sc_narrow_kernel_km1(int nb);
 sc::NarrowFn sc_narrow_kernel_km2(int nb);
 sc::NarrowFn sc_narrow_kernel_km3(int nb);

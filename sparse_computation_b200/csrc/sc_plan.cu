@@ -54,6 +54,7 @@ struct sc_plan {
   const int32_t *item_ptr = nullptr;
   const int32_t *order = nullptr;
   float *stage_b = nullptr, *stage_c = nullptr;
+  std::vector<int64_t> work;  // per local panel, for batch scheduling
   ~sc_plan() {
     if (dev || stage_b || stage_c) {
       int prev;
@@ -72,14 +73,14 @@ namespace {
 using sc::WideFn;
 using sc::NarrowFn;
 
-WideFn wide_kernel(int km, int vec) {
+WideFn wide_kernel(int km, int vec, bool batch) {
   switch (km) {
-    case 1: return sc_wide_kernel_km1(vec);
-    case 2: return sc_wide_kernel_km2(vec);
-    case 3: return sc_wide_kernel_km3(vec);
-    case 4: return sc_wide_kernel_km4(vec);
-    case 5: return sc_wide_kernel_km5(vec);
-    default: return sc_wide_kernel_km6(vec);
+    case 1: return sc_wide_kernel_km1(vec, batch);
+    case 2: return sc_wide_kernel_km2(vec, batch);
+    case 3: return sc_wide_kernel_km3(vec, batch);
+    case 4: return sc_wide_kernel_km4(vec, batch);
+    case 5: return sc_wide_kernel_km5(vec, batch);
+    default: return sc_wide_kernel_km6(vec, batch);
   }
 }
 
@@ -196,6 +197,7 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   std::vector<int32_t> order(plan->panels);
   for (int64_t i = 0; i < plan->panels; ++i) order[i] = (int32_t)i;
   std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return work[a] > work[b]; });
+  plan->work = work;
 
   // Kernel family and CTA shape.
   int slices = 1;
@@ -243,6 +245,21 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
 
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+sc::WideArgs wide_args(const sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc) {
+  require(ldb <= (int64_t)(UINT32_MAX / 4), SC_ERR_UNSUPPORTED, "ldb too large (row pitch must be < 4 GiB)");
+  sc::WideArgs a;
+  a.recs = p->recs;
+  a.items = p->item_list;
+  a.item_ptr = p->item_ptr;
+  a.B = B;
+  a.C = C;
+  a.ldc = ldc;
+  a.rows = p->rows;
+  a.ldb_bytes = (uint32_t)(ldb * 4);
+  a.n_cols = (int)p->n;
+  return a;
+}
+
 void launch(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int accumulate,
             cudaStream_t stream) {
   require(ldb >= p->n && ldc >= p->n, SC_ERR_ARG, "leading dimension smaller than n_cols_b");
@@ -261,11 +278,10 @@ void launch(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int 
                         aligned(C, 4 * vec)))
       vec >>= 1;
     const int slices = (int)((p->n + 32 * vec - 1) / (32 * vec));
-    WideFn fn = wide_kernel((int)p->km, vec);
-    const size_t smem = (size_t)(p->warps - 1) * p->km * 32 * vec * sizeof(float);
-    fn<<<dim3((unsigned)p->panels, slices), threads, smem, stream>>>(p->recs, p->item_list, p->item_ptr,
-                                                                     p->order, B, ldb, C, ldc, p->rows,
-                                                                     (int)p->n, accumulate);
+    WideFn fn = wide_kernel((int)p->km, vec, false);
+    const size_t smem = sc::wide_smem_bytes(p->warps, (int)p->km, vec);
+    fn<<<dim3((unsigned)p->panels, slices), threads, smem, stream>>>(wide_args(p, B, ldb, C, ldc), nullptr,
+                                                                     p->order, accumulate);
   }
   cuda_check(cudaGetLastError(), "kernel launch");
 }
@@ -356,5 +372,119 @@ int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream) {
 }
 
 void sc_plan_free(sc_plan *p) { delete p; }
+
+}  // extern "C"
+
+// A set of plans (same device, kernel_m and B width) run as one launch: one
+// CTA per (matrix, panel), heaviest panels first across all matrices.
+struct sc_batch {
+  int device = 0;
+  int km = 0, vec = 1, warps = 1, slices = 1;
+  int64_t n = 0;
+  std::vector<sc_plan *> plans;
+  int64_t tasks = 0;
+  void *dev = nullptr;           // descs | order
+  sc::WideArgs *descs = nullptr;
+  int2 *order = nullptr;
+  bool bound = false;
+  ~sc_batch() {
+    if (dev) {
+      int prev;
+      bool ok = cudaGetDevice(&prev) == cudaSuccess;
+      if (ok && prev != device) cudaSetDevice(device);
+      cudaFree(dev);
+      if (ok && prev != device) cudaSetDevice(prev);
+    }
+  }
+};
+
+extern "C" {
+
+int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out) {
+  SC_API_BEGIN
+  require(plans != nullptr && out != nullptr && count >= 1, SC_ERR_ARG, "need at least one plan");
+  auto b = std::make_unique<sc_batch>();
+  const sc_plan *p0 = plans[0];
+  require(p0 != nullptr, SC_ERR_ARG, "null plan");
+  b->device = p0->device;
+  b->km = (int)p0->km;
+  b->n = p0->n;
+  require(p0->kernel == 2, SC_ERR_UNSUPPORTED, "batches run the wide-B kernel (n_cols_b not in {1, 2, 4})");
+  b->vec = p0->vec;
+  b->slices = (int)((b->n + 32 * b->vec - 1) / (32 * b->vec));
+  std::vector<std::pair<int64_t, int2>> tasks;
+  for (int32_t i = 0; i < count; ++i) {
+    const sc_plan *p = plans[i];
+    require(p != nullptr, SC_ERR_ARG, "null plan");
+    require(p->device == b->device && p->km == b->km && p->n == b->n, SC_ERR_UNSUPPORTED,
+            "plans of a batch must share device, kernel_m and n_cols_b");
+    b->plans.push_back(plans[i]);
+    for (int64_t lp = 0; lp < p->panels; ++lp) tasks.push_back({p->work[lp], make_int2(i, (int)lp)});
+  }
+  std::stable_sort(tasks.begin(), tasks.end(),
+                   [](const std::pair<int64_t, int2> &x, const std::pair<int64_t, int2> &y) { return x.first > y.first; });
+  b->tasks = (int64_t)tasks.size();
+  int64_t items = 0;
+  for (auto *p : b->plans) items += p->items;
+  {
+    int64_t units = std::max<int64_t>(1, b->tasks * b->slices);
+    int w = pow2_at_least((kTargetWarps + units - 1) / units);
+    int64_t avg_items = b->tasks ? (items + b->tasks - 1) / b->tasks : 1;
+    w = std::min(w, pow2_at_least(std::max<int64_t>(1, avg_items)));
+    b->warps = std::max(1, std::min(w, 8));
+  }
+  DeviceGuard dg(b->device);
+  const size_t bd = ((count * sizeof(sc::WideArgs)) + 255) & ~(size_t)255;
+  const size_t bo = std::max<size_t>(1, tasks.size()) * sizeof(int2);
+  cuda_check(cudaMalloc(&b->dev, bd + bo), "cudaMalloc(batch)");
+  b->descs = reinterpret_cast<sc::WideArgs *>(b->dev);
+  b->order = reinterpret_cast<int2 *>(static_cast<char *>(b->dev) + bd);
+  std::vector<int2> ord(tasks.size());
+  for (size_t i = 0; i < tasks.size(); ++i) ord[i] = tasks[i].second;
+  if (!ord.empty())
+    cuda_check(cudaMemcpy(b->order, ord.data(), ord.size() * sizeof(int2), cudaMemcpyHostToDevice),
+               "upload batch order");
+  *out = b.release();
+  SC_API_END
+}
+
+int sc_batch_bind(sc_batch *b, const float *const *dB, const int64_t *ldb, float *const *dC,
+                  const int64_t *ldc) {
+  SC_API_BEGIN
+  require(b != nullptr && dB != nullptr && dC != nullptr && ldb != nullptr && ldc != nullptr, SC_ERR_ARG,
+          "null argument");
+  std::vector<sc::WideArgs> d(b->plans.size());
+  for (size_t i = 0; i < b->plans.size(); ++i) {
+    const sc_plan *p = b->plans[i];
+    require(ldb[i] >= p->n && ldc[i] >= p->n, SC_ERR_ARG, "leading dimension smaller than n_cols_b");
+    require(p->rows == 0 || (dB[i] != nullptr && dC[i] != nullptr), SC_ERR_ARG, "null B or C");
+    require(ldb[i] % b->vec == 0 && ldc[i] % b->vec == 0 && aligned(dB[i], 4 * b->vec) &&
+                aligned(dC[i], 4 * b->vec),
+            SC_ERR_ARG, "batch operands must be aligned to the vector width (16 bytes for n_cols_b >= 128)");
+    d[i] = wide_args(p, dB[i], ldb[i], dC[i], ldc[i]);
+  }
+  DeviceGuard dg(b->device);
+  cuda_check(cudaMemcpy(b->descs, d.data(), d.size() * sizeof(sc::WideArgs), cudaMemcpyHostToDevice),
+             "upload batch operands");
+  b->bound = true;
+  SC_API_END
+}
+
+int sc_batch_spmm(sc_batch *b, int32_t accumulate, void *stream) {
+  SC_API_BEGIN
+  require(b != nullptr, SC_ERR_ARG, "null batch");
+  require(b->bound, SC_ERR_ARG, "sc_batch_bind must be called before sc_batch_spmm");
+  if (b->tasks == 0) return SC_OK;
+  DeviceGuard dg(b->device);
+  WideFn fn = wide_kernel(b->km, b->vec, true);
+  sc::WideArgs none{};
+  fn<<<dim3((unsigned)b->tasks, b->slices), 32 * b->warps, sc::wide_smem_bytes(b->warps, b->km, b->vec),
+       static_cast<cudaStream_t>(stream)>>>(none, b->descs, reinterpret_cast<const int32_t *>(b->order),
+                                            accumulate);
+  cuda_check(cudaGetLastError(), "kernel launch");
+  SC_API_END
+}
+
+void sc_batch_free(sc_batch *b) { delete b; }
 
 }  // extern "C"

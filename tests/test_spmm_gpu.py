@@ -210,3 +210,38 @@ def test_config5_full_size_properties(cuda):
         p.spmm(Bt, Cs[r[0] * 4: r[1] * 4])
     torch.cuda.synchronize()
     assert torch.allclose(Cs, C, rtol=1e-5, atol=1e-6)
+
+
+def test_batch_layer_stack_one_launch(cuda):
+    """All 96 weights of config 4 in one launch == the oracle for each."""
+    import torch
+    mats = wl.config4(128)
+    plans, Bs, Cs = [], [], []
+    for name, a, B in mats:
+        cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+        plans.append(sc.SpMMPlan(cf, 128))
+        Bs.append(torch.from_numpy(B).to(cuda))
+        Cs.append(torch.full((a[0], 128), float("nan"), device=cuda))
+    batch = sc.SpMMBatch(plans)
+    batch.bind(Bs, Cs)
+    for _ in range(2):
+        batch.spmm()
+    torch.cuda.synchronize()
+    for (name, a, B), C in zip(mats, Cs):
+        assert_parity(C.cpu().numpy(), a, B)
+    # accumulate doubles the product
+    batch.spmm(accumulate=True)
+    torch.cuda.synchronize()
+    for (name, a, B), C in zip(mats[:5], Cs[:5]):
+        assert_parity(C.cpu().numpy() / 2, a, B)
+
+
+def test_batch_rejects_mixed_plans(cuda):
+    a, _ = wl.config1()
+    h = to_csr_handle(a)
+    p1 = sc.SpMMPlan(sc.csr_to_compressed_format_converter(h, 4, 1), 128)
+    p2 = sc.SpMMPlan(sc.csr_to_compressed_format_converter(h, 2, 1), 128)
+    p3 = sc.SpMMPlan(sc.csr_to_compressed_format_converter(h, 4, 1), 4)
+    for bad in ([p1, p2], [p3]):
+        with pytest.raises(sc.ScError):
+            sc.SpMMBatch(bad)
