@@ -7,6 +7,7 @@
 // contiguous allocation holding a flat record stream and a work list.
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -101,7 +102,16 @@ int pow2_at_least(int64_t x) {
   return p;
 }
 
-constexpr int64_t kTargetWarps = 148 * 32;  // B200: 148 SMs, ~half of the 64 warp slots
+// Warps the schedule aims to put in flight (B200: 148 SMs); SC_TARGET_WARPS
+// overrides it for tuning experiments.
+int64_t target_warps() {
+  static const int64_t v = [] {
+    const char *e = getenv("SC_TARGET_WARPS");
+    long long x = e ? atoll(e) : 0;
+    return (int64_t)(x > 0 ? x : 148 * 64);
+  }();
+  return v;
+}
 
 sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int64_t pe) {
   const int km = cf.kernel_m;
@@ -210,7 +220,7 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   }
   {
     int64_t units = std::max<int64_t>(1, plan->panels * slices);
-    int w = pow2_at_least((kTargetWarps + units - 1) / units);
+    int w = pow2_at_least((target_warps() + units - 1) / units);
     int64_t avg_items = plan->panels ? (plan->items + plan->panels - 1) / plan->panels : 1;
     w = std::min(w, pow2_at_least(std::max<int64_t>(1, avg_items)));
     plan->warps = std::max(1, std::min(w, 8));
@@ -428,7 +438,7 @@ int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out) {
   for (auto *p : b->plans) items += p->items;
   {
     int64_t units = std::max<int64_t>(1, b->tasks * b->slices);
-    int w = pow2_at_least((kTargetWarps + units - 1) / units);
+    int w = pow2_at_least((target_warps() + units - 1) / units);
     int64_t avg_items = b->tasks ? (items + b->tasks - 1) / b->tasks : 1;
     w = std::min(w, pow2_at_least(std::max<int64_t>(1, avg_items)));
     b->warps = std::max(1, std::min(w, 8));
