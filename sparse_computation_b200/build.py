@@ -71,7 +71,27 @@ def build(verbose: bool = False, force: bool = False) -> str:
     if force or jobs or not _newer(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-Xcompiler", "-fPIC", "-Xlinker",
               "--exclude-libs,ALL", *objs, "-o", LIB, "-lpthread"])
+    build_apps(force=force)
     return LIB
+
+
+APPS = {"spmm_demo_gpu": 0, "spmm_small_b_col_demo_gpu": 1, "spmv_demo_gpu": 2}
+BIN = os.path.join(PKG, "bin")
+
+
+def build_apps(force: bool = False) -> None:
+    """The three demo executables (reference command line) in sparse_computation_b200/bin/."""
+    os.makedirs(BIN, exist_ok=True)
+    src = os.path.join(PKG, "apps", "sc_demo.cu")
+    jobs = []
+    for name, mode in APPS.items():
+        out = os.path.join(BIN, name)
+        if force or not _newer(out, [src, LIB, os.path.join(INCLUDE, "sc_b200.h")]):
+            jobs.append([NVCC, *ARCH, "-O2", "-std=c++17", f"-DSC_DEMO_MODE={mode}", "-I", INCLUDE, src,
+                         "-o", out, "-L", os.path.dirname(LIB), "-l:" + os.path.basename(LIB),
+                         "-Xlinker", "-rpath,$ORIGIN/..", "-lcusparse", "-lcublas"])
+    with ThreadPoolExecutor(max_workers=3) as ex:
+        list(ex.map(_run, jobs))
 
 
 if __name__ == "__main__":
