@@ -78,26 +78,7 @@ def workload(cfg: int, n_cols_b):
     return f"config4: 96-matrix transformer-base stack 80%, B Kx{N}", [(a, B) for _, a, B in wl.config4(N)]
 
 
-def row_slice(a, r0, r1):
-    m, n, ip, ix, dx = a
-    s, e = ip[r0], ip[r1]
-    return r1 - r0, n, (ip[r0:r1 + 1] - s).astype(np.int32), ix[s:e], dx[s:e]
-
-
-def balanced_panel_cuts(indptr, m_rows, km, world):
-    """Row-panel boundaries splitting the nonzeros into `world` near-equal shares."""
-    panels = (m_rows + km - 1) // km
-    ends = np.minimum(np.arange(1, panels + 1) * km, m_rows)
-    cum = indptr[ends].astype(np.int64)
-    total = cum[-1] if panels else 0
-    cuts = [0]
-    for r in range(1, world):
-        cuts.append(int(np.searchsorted(cum, total * r / world)) + 1 if total else panels * r // world)
-    cuts.append(panels)
-    cuts = [min(max(c, 0), panels) for c in cuts]
-    for i in range(1, len(cuts)):
-        cuts[i] = max(cuts[i], cuts[i - 1])
-    return cuts
+from sparse_computation_b200.partition import balanced_panel_cuts, lpt_assign, row_slice  # noqa: E402
 
 
 # ---------------------------------------------------------------- clocks --
@@ -314,14 +295,8 @@ def main():
     jobs = []
     total_nnz = sum(len(a[3]) for a, _ in mats)
     if layers:
-        # greedy LPT assignment of whole matrices to ranks by nonzeros
-        load = [0] * world
-        owner = []
-        for i in sorted(range(len(mats)), key=lambda i: -len(mats[i][0][3])):
-            r = min(range(world), key=lambda r: load[r])
-            load[r] += len(mats[i][0][3])
-            owner.append((i, r))
-        mine = sorted(i for i, r in owner if r == rank)
+        owner = lpt_assign([len(a[3]) for a, _ in mats], world)
+        mine = [i for i, r in enumerate(owner) if r == rank]
         for i in mine:
             a, B = mats[i]
             cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*a), km, kn)
