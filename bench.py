@@ -49,6 +49,9 @@ def parse():
     p.add_argument("--kernel-m", type=int, default=4)
     p.add_argument("--kernel-n", type=int, default=1)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                   help="N>1 row partition: C blocks stored to peers by the SpMM kernel itself over NVLink "
+                        "(symmetric memory) or gathered afterwards with NCCL all-gather")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU work of the bounded cpu_baseline sample")
     return p.parse_args()
@@ -79,6 +82,22 @@ def workload(cfg: int, n_cols_b):
 
 
 from sparse_computation_b200.partition import balanced_panel_cuts, lpt_assign, row_slice  # noqa: E402
+
+
+def symmetric_buffer(shape, dev):
+    """A float32 buffer allocated in torch symmetric memory (peer-mapped on
+    every rank) and its rendezvous handle."""
+    import torch
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+    group = dist.group.WORLD
+    try:
+        symm_mem.enable_symm_mem_for_group(group.group_name)
+    except Exception:
+        pass
+    t = symm_mem.empty(shape, dtype=torch.float32, device=dev)
+    hdl = symm_mem.rendezvous(t, group.group_name)
+    return t, hdl
 
 
 # ---------------------------------------------------------------- clocks --
@@ -316,8 +335,14 @@ def main():
             max_rows = max(min(cuts[r + 1] * km, m) - min(cuts[r] * km, m) for r in range(world))
             j = {"plan": plan, "B": torch.from_numpy(B).to(dev), "rows": r1 - r0, "max_rows": max_rows,
                  "m": m, "nnz_local": len(blk[3]), "Bhost": B, "cuts": cuts, "K": a[1]}
-            j["gather"] = torch.empty((world, max_rows, N), device=dev)
-            j["C"] = j["gather"][rank, : j["rows"]] if world > 1 else torch.empty((j["rows"], N), device=dev)
+            if world > 1 and args.exchange == "peer":
+                full, hdl = symmetric_buffer((m, N), dev)
+                j["full"], j["hdl"] = full, hdl
+                j["C"] = full[r0:r1]
+                j["peers"] = [int(hdl.buffer_ptrs[q]) + r0 * N * 4 for q in range(world) if q != rank]
+            else:
+                j["gather"] = torch.empty((world, max_rows, N), device=dev)
+                j["C"] = j["gather"][rank, : j["rows"]] if world > 1 else torch.empty((j["rows"], N), device=dev)
             jobs.append(j)
     batch = None
     if len(jobs) > 1 and jobs[0]["plan"].info["kernel"] == 2:
@@ -325,15 +350,23 @@ def main():
         batch.bind([j["B"] for j in jobs], [j["C"] for j in jobs])
     t_setup = time.perf_counter() - t_setup
 
+    peer_mode = world > 1 and not layers and args.exchange == "peer"
+
     def launch_all(stream):
         if batch is not None:
             batch.spmm(stream=stream)  # every local matrix in one kernel launch
         else:
             for j in jobs:
-                j["plan"].spmm(j["B"], j["C"], stream=stream)
+                if peer_mode:  # the kernel stores each C tile locally and into every peer's C
+                    j["plan"].spmm_peers(j["B"], j["C"], j["peers"], stream=stream)
+                else:
+                    j["plan"].spmm(j["B"], j["C"], stream=stream)
 
     def gather_all():
-        if world > 1 and not layers:
+        if peer_mode:
+            for j in jobs:
+                j["hdl"].barrier(channel=0)  # all ranks' peer stores have landed
+        elif world > 1 and not layers:
             for j in jobs:
                 # in place: this rank's block already sits at its slot
                 dist.all_gather_into_tensor(j["gather"], j["gather"][rank])
@@ -402,6 +435,9 @@ def main():
                 if layers:
                     for j, hC in zip(jobs, hCs):
                         hC.copy_(j["C"], non_blocking=True)
+                elif rank == 0 and peer_mode:
+                    for j, hC in zip(jobs, hCs):
+                        hC.copy_(j["full"], non_blocking=True)
                 elif rank == 0:
                     for j, hC in zip(jobs, hCs):
                         for r in range(world):
@@ -457,7 +493,10 @@ def main():
         "config": {"workload": name, "coarsening": [km, kn], "n_cols_b": N, "nnz": total_nnz,
                    "parallelism": ("1 GPU" if world == 1 else
                                    f"whole matrices sharded over {world} GPUs (LPT by nnz), no collective"
-                                   if layers else f"row-partition x{world} + NCCL all-gather of C"),
+                                   if layers else
+                                   (f"row-partition x{world}; SpMM kernel stores C tiles into every peer over "
+                                    "NVLink (symmetric memory) + one barrier" if peer_mode else
+                                    f"row-partition x{world} + NCCL all-gather of C")),
                    "launches_per_step": 1 if batch is not None else len(jobs),
                    "l2": "flushed before every timed step (256 MiB write, outside the events)",
                    "plan": {k: info[k] for k in ("entries", "items", "kernel", "warps_per_panel",

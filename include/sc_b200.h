@@ -137,6 +137,17 @@ int sc_plan_get_info(const sc_plan *p, sc_plan_info *info);
  * reference kernels' C += A*B with atomics (which needed a zeroed C). */
 int sc_spmm(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc,
             int32_t accumulate, void *stream);
+/* sc_spmm that also stores every C tile into `npeers` (<= 7) peer buffers:
+ * other GPUs' copies of C mapped into this process (CUDA IPC / symmetric
+ * memory), same layout and ldc, each pointer addressing the same first row as
+ * dC.  With A row-partitioned over GPUs (sc_plan_create_panels) and each
+ * rank passing its peers' full-C buffers offset to its own rows, the kernel
+ * itself performs the all-gather of the C row blocks over NVLink, overlapped
+ * with the computation; the caller then runs one cross-GPU barrier on the
+ * stream before reading C.  Wide-B plans only.  The reference has no
+ * multi-GPU path; this replaces "SpMM then NCCL all-gather". */
+int sc_spmm_peers(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc, float *const *peer_C,
+                  int32_t npeers, int32_t accumulate, void *stream);
 /* y = A*x or y += A*x (plan built with n_cols_b == 1). */
 int sc_spmv(sc_plan *p, const float *dx, float *dy, int32_t accumulate, void *stream);
 /* End-to-end product from HOST buffers: copies hB (K x N, dense row-major)

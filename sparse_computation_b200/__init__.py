@@ -49,7 +49,7 @@ EXPORTED_SYMBOLS = (
     "sc_cf_pattern_sizes", "sc_cf_pattern_arrays", "sc_cf_real_nnz", "sc_cf_free",
     "sc_companion_mtx_path",
     "sc_plan_create", "sc_plan_create_panels", "sc_plan_get_info", "sc_spmm", "sc_spmv",
-    "sc_spmm_host", "sc_plan_free",
+    "sc_spmm_host", "sc_plan_free", "sc_spmm_peers",
     "sc_batch_create", "sc_batch_bind", "sc_batch_spmm", "sc_batch_free",
 )
 
@@ -106,6 +106,7 @@ def lib() -> ctypes.CDLL:
         "sc_plan_get_info": ([vp, P(_PlanInfo)], ctypes.c_int),
         "sc_spmm": ([vp, vp, i64, vp, i64, i32, vp], ctypes.c_int),
         "sc_spmv": ([vp, vp, vp, i32, vp], ctypes.c_int),
+        "sc_spmm_peers": ([vp, vp, i64, vp, i64, vp, i32, i32, vp], ctypes.c_int),
         "sc_spmm_host": ([vp, vp, vp, vp], ctypes.c_int),
         "sc_plan_free": ([vp], None),
         "sc_batch_create": ([vp, i32, P(vp)], ctypes.c_int),
@@ -359,6 +360,20 @@ class SpMMPlan:
         _check(lib().sc_spmm(self._h, ctypes.c_void_p(B.data_ptr()), B.stride(0),
                              ctypes.c_void_p(C.data_ptr()), C.stride(0), 1 if accumulate else 0,
                              self._stream(stream)))
+        return C
+
+    def spmm_peers(self, B, C, peer_ptrs, accumulate: bool = False, stream=None):
+        """spmm() that also stores C into peer GPUs' buffers (device addresses
+        `peer_ptrs`, each pointing at the same first row as C)."""
+        torch = _torch()
+        if B.dtype != torch.float32 or C.dtype != torch.float32 or B.stride(1) != 1 or C.stride(1) != 1:
+            raise ScError(SC_ERR_ARG, "B and C must be float32 with unit column stride")
+        if tuple(B.shape) != (self.cols, self.n) or tuple(C.shape) != (self.rows, self.n):
+            raise ScError(SC_ERR_ARG, "operand shapes do not match the plan")
+        arr = (ctypes.c_void_p * max(1, len(peer_ptrs)))(*peer_ptrs)
+        _check(lib().sc_spmm_peers(self._h, ctypes.c_void_p(B.data_ptr()), B.stride(0),
+                                   ctypes.c_void_p(C.data_ptr()), C.stride(0), arr, len(peer_ptrs),
+                                   1 if accumulate else 0, self._stream(stream)))
         return C
 
     def spmv(self, x, y=None, accumulate: bool = False, stream=None):

@@ -101,6 +101,8 @@ __device__ __forceinline__ void load_rec(const uint32_t *__restrict__ r, int &co
 // address formed with one 32x32->64 multiply-add, and U entries' B rows are
 // loaded (U independent 32*VEC-wide loads in flight) before the P*VEC FMAs.
 
+constexpr int kMaxPeers = 7;
+
 // Operands of one matrix for the wide kernel.
 struct WideArgs {
   const uint32_t *recs;
@@ -112,6 +114,11 @@ struct WideArgs {
   int64_t rows;
   uint32_t ldb_bytes;  // row pitch of B in bytes (< 4 GiB)
   int n_cols;
+  // Peer copies of C (other GPUs' buffers mapped into this address space,
+  // same layout and ldc): every C tile is also stored there, so the row
+  // blocks of a row-partitioned product are exchanged by the kernel itself.
+  int npeers;
+  float *peers[kMaxPeers];
 };
 
 #ifndef SC_WIDE_U
@@ -289,13 +296,17 @@ spmm_wide_kernel(WideArgs one, const WideArgs *__restrict__ many, const int32_t 
   for (int k = 0; k < KM; ++k) {
     const int64_t row = (int64_t)panel * KM + k;
     if (row >= one.rows) break;
-    float *c = one.C + row * one.ldc + col0;
+    const int64_t off = row * one.ldc + col0;
+    float *c = one.C + off;
     if constexpr (VEC == 1) {
-      c[0] = accumulate ? c[0] + acc[k][0] : acc[k][0];
+      const float o = accumulate ? c[0] + acc[k][0] : acc[k][0];
+      c[0] = o;
+      for (int p = 0; p < one.npeers; ++p) one.peers[p][off] = o;
     } else if constexpr (VEC == 2) {
       float2 o = make_float2(acc[k][0], acc[k][1]);
       if (accumulate) { float2 x = *reinterpret_cast<float2 *>(c); o.x += x.x; o.y += x.y; }
       *reinterpret_cast<float2 *>(c) = o;
+      for (int p = 0; p < one.npeers; ++p) *reinterpret_cast<float2 *>(one.peers[p] + off) = o;
     } else {
       float4 o = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
       if (accumulate) {
@@ -303,8 +314,12 @@ spmm_wide_kernel(WideArgs one, const WideArgs *__restrict__ many, const int32_t 
         o.x += x.x; o.y += x.y; o.z += x.z; o.w += x.w;
       }
       *reinterpret_cast<float4 *>(c) = o;
+      for (int p = 0; p < one.npeers; ++p) *reinterpret_cast<float4 *>(one.peers[p] + off) = o;
     }
   }
+  // Peer stores must be visible system-wide before the caller's cross-GPU
+  // barrier releases the other ranks.
+  if (one.npeers > 0) __threadfence_system();
 }
 
 // ------------------------------------------------------------ narrow B ----

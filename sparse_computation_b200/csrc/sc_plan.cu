@@ -267,6 +267,8 @@ sc::WideArgs wide_args(const sc_plan *p, const float *B, int64_t ldb, float *C, 
   a.rows = p->rows;
   a.ldb_bytes = (uint32_t)(ldb * 4);
   a.n_cols = (int)p->n;
+  a.npeers = 0;
+  for (int i = 0; i < sc::kMaxPeers; ++i) a.peers[i] = nullptr;
   return a;
 }
 
@@ -354,6 +356,35 @@ int sc_spmm(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc, in
   SC_API_BEGIN
   require(p != nullptr, SC_ERR_ARG, "null plan");
   launch(p, dB, ldb, dC, ldc, accumulate, static_cast<cudaStream_t>(stream));
+  SC_API_END
+}
+
+int sc_spmm_peers(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc, float *const *peer_C,
+                  int32_t npeers, int32_t accumulate, void *stream) {
+  SC_API_BEGIN
+  require(p != nullptr, SC_ERR_ARG, "null plan");
+  require(npeers >= 0 && npeers <= sc::kMaxPeers, SC_ERR_ARG, "npeers must be 0..7");
+  require(npeers == 0 || peer_C != nullptr, SC_ERR_ARG, "null peer list");
+  require(p->kernel == 2, SC_ERR_UNSUPPORTED, "peer stores are implemented for the wide-B kernel (N not in {1,2,4})");
+  require(ldb >= p->n && ldc >= p->n, SC_ERR_ARG, "leading dimension smaller than n_cols_b");
+  if (p->panels == 0 || p->rows == 0) return SC_OK;
+  require(dB != nullptr && dC != nullptr, SC_ERR_ARG, "null B or C");
+  int vec = p->vec;
+  bool al = true;
+  for (int i = 0; i < npeers; ++i) al = al && peer_C[i] != nullptr && aligned(peer_C[i], 4 * vec);
+  require(al, SC_ERR_ARG, "peer C pointers must be non-null and aligned like C");
+  while (vec > 1 && !(p->n % vec == 0 && ldb % vec == 0 && ldc % vec == 0 && aligned(dB, 4 * vec) &&
+                      aligned(dC, 4 * vec)))
+    vec >>= 1;
+  DeviceGuard dg(p->device);
+  sc::WideArgs a = wide_args(p, dB, ldb, dC, ldc);
+  a.npeers = npeers;
+  for (int i = 0; i < npeers; ++i) a.peers[i] = peer_C[i];
+  const int slices = (int)((p->n + 32 * vec - 1) / (32 * vec));
+  WideFn fn = wide_kernel((int)p->km, vec, false);
+  fn<<<dim3((unsigned)p->panels, slices), 32 * p->warps, sc::wide_smem_bytes(p->warps, (int)p->km, vec),
+       static_cast<cudaStream_t>(stream)>>>(a, nullptr, p->order, accumulate);
+  cuda_check(cudaGetLastError(), "kernel launch");
   SC_API_END
 }
 

@@ -245,3 +245,25 @@ def test_batch_rejects_mixed_plans(cuda):
     for bad in ([p1, p2], [p3]):
         with pytest.raises(sc.ScError):
             sc.SpMMBatch(bad)
+
+
+def test_peer_store_epilogue_single_gpu(cuda):
+    """sc_spmm_peers with 'peers' that are other buffers on the same GPU: each
+    receives exactly the tile written to C."""
+    import torch
+    a, B = wl.config3((2048, 512), 128)
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+    plan = sc.SpMMPlan(cf, 128, panel_range=(100, 300))
+    Bt = torch.from_numpy(B).to(cuda)
+    full = [torch.full((2048, 128), -1.0, device=cuda) for _ in range(4)]
+    C = full[0][400:1200]
+    peers = [f.data_ptr() + 400 * 128 * 4 for f in full[1:]]
+    plan.spmm_peers(Bt, C, peers)
+    torch.cuda.synchronize()
+    for f in full[1:]:
+        assert torch.equal(f, full[0])
+    assert torch.all(full[0][:400] == -1) and torch.all(full[0][1200:] == -1)
+    rows = np.arange(400, 1200)
+    assert_parity(C.cpu().numpy(), a, B, rows=rows)
+    with pytest.raises(sc.ScError):
+        sc.SpMMPlan(cf, 4).spmm_peers(torch.zeros((512, 4), device=cuda), torch.zeros((2048, 4), device=cuda), peers)
