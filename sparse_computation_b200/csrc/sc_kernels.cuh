@@ -317,9 +317,10 @@ spmm_wide_kernel(WideArgs one, const WideArgs *__restrict__ many, const int32_t 
       for (int p = 0; p < one.npeers; ++p) *reinterpret_cast<float4 *>(one.peers[p] + off) = o;
     }
   }
-  // Peer stores must be visible system-wide before the caller's cross-GPU
-  // barrier releases the other ranks.
-  if (one.npeers > 0) __threadfence_system();
+  // No fence here: the peer stores are complete when the kernel completes,
+  // and the caller's cross-GPU barrier (stream-ordered after this kernel)
+  // publishes them; a per-thread system fence would hold every CTA until its
+  // remote stores were acknowledged.
 }
 
 // ------------------------------------------------------------ narrow B ----
