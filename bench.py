@@ -49,6 +49,9 @@ def parse():
     p.add_argument("--kernel-m", type=int, default=4)
     p.add_argument("--kernel-n", type=int, default=1)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--sweep-small", action="store_true",
+                   help="config 2 table: every sparsity x N in {1,2,4}, single warm launch, CUDA-graph "
+                        "replay, and cuSPARSE (one JSON line with a 'sweep' list)")
     p.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                    help="N>1 row partition: C blocks stored to peers by the SpMM kernel itself over NVLink "
                         "(symmetric memory) or gathered afterwards with NCCL all-gather")
@@ -254,6 +257,64 @@ def cusparse_baseline(mats, dev, flush, args):
         return {"unavailable": str(ex)[:200]}
 
 
+def small_b_sweep(args):
+    """512x512 magnitude-pruned weights (config 2) at every sparsity, N in
+    {1, 2, 4}: our kernel as one warm launch (L2-resident, as in serving) and
+    as 200 launches replayed from one CUDA graph, next to cuSPARSE CSR SpMM
+    launched back to back."""
+    import torch
+
+    import sparse_computation_b200 as sc
+    from sparse_computation_b200 import workloads as wl
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    reps = 200
+
+    def events_ms(fn, n):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        fn()
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        e.synchronize()
+        return s.elapsed_time(e) / n
+
+    rows = []
+    for sp in wl.CONFIG2_SPARSITIES:
+        for N in (1, 2, 4):
+            a, B = wl.config2(sp, N)
+            m, n, ip, ix, dx = a
+            cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*a), args.kernel_m, args.kernel_n)
+            plan = sc.SpMMPlan(cf, N, device=0)
+            Bt = torch.from_numpy(B).to(dev)
+            C = torch.empty((m, N), device=dev)
+            ours = events_ms(lambda: plan.spmm(Bt, C, stream=stream), reps)
+            g = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(dev)
+            with torch.cuda.stream(side):
+                plan.spmm(Bt, C, stream=side)
+                torch.cuda.synchronize()
+                with torch.cuda.graph(g, stream=side):
+                    for _ in range(reps):
+                        plan.spmm(Bt, C, stream=side)
+            graph = events_ms(g.replay, 5) / reps
+            A = torch.sparse_csr_tensor(torch.from_numpy(ip.astype(np.int32)), torch.from_numpy(ix.astype(np.int32)),
+                                        torch.from_numpy(dx.astype(np.float32)), size=(m, n)).to(dev)
+            Bc = Bt if N > 1 else Bt.view(n, 1)
+            cus = events_ms(lambda: A @ Bc, reps)
+            fl = 2.0 * len(ix) * N
+            rows.append({"sparsity": sp, "n_cols_b": N, "nnz": int(len(ix)),
+                         "ours_us": ours * 1e3, "ours_graph_us": graph * 1e3, "cusparse_us": cus * 1e3,
+                         "ours_gflops": fl / (ours * 1e-3) / 1e9, "ours_graph_gflops": fl / (graph * 1e-3) / 1e9,
+                         "cusparse_gflops": fl / (cus * 1e-3) / 1e9, "speedup_vs_cusparse": cus / ours,
+                         "graph_speedup_vs_cusparse": cus / graph})
+    print(json.dumps({"metric": "SpMM GFLOP/s (2*nnz*N)", "unit": "GFLOP/s", "config": {
+        "workload": "config2 sweep: A 512x512 magnitude-pruned N(0,0.05^2), B 512xN",
+        "coarsening": [args.kernel_m, args.kernel_n], "l2": "warm (L2-resident)"}, "sweep": rows}), flush=True)
+
+
 # ----------------------------------------------------------- reference ---
 
 def run_reference(args, rank):
@@ -297,6 +358,10 @@ def main():
     import torch.distributed as dist
 
     import sparse_computation_b200 as sc
+
+    if args.sweep_small:
+        small_b_sweep(args)
+        return
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
