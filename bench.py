@@ -46,7 +46,8 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--config", type=int, default=5, choices=[1, 2, 3, 4, 5])
     p.add_argument("--n-cols-b", type=int, default=None)
-    p.add_argument("--kernel-m", type=int, default=4)
+    p.add_argument("--kernel-m", default="4",
+                   help="coarsening rows, or 'auto' to time kernel_m 1..6 per matrix and keep the fastest")
     p.add_argument("--kernel-n", type=int, default=1)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--sweep-small", action="store_true",
@@ -370,7 +371,8 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
 
     name, mats = workload(args.config, args.n_cols_b)
-    km, kn = args.kernel_m, args.kernel_n
+    auto_m = args.kernel_m == "auto"
+    km, kn = (4 if auto_m else int(args.kernel_m)), args.kernel_n
     N = mats[0][1].shape[1]
 
     # ---- setup: this rank's row blocks, coarsening, plans (untimed)
@@ -378,27 +380,40 @@ def main():
     layers = args.config == 4  # independent matrices: shard whole matrices, no collective
     jobs = []
     total_nnz = sum(len(a[3]) for a, _ in mats)
+    tuned = {}
+
+    def pick_m(i, a):
+        """kernel_m of matrix i: fixed, or measured per matrix (--kernel-m auto)."""
+        if not auto_m:
+            return km
+        if i not in tuned:
+            from sparse_computation_b200 import tuning
+            tuned[i] = tuning.autotune_kernel_m(sc.CSR.from_arrays(*a), N, device=local)[0]
+        return tuned[i]
+
     if layers:
         owner = lpt_assign([len(a[3]) for a, _ in mats], world)
         mine = [i for i, r in enumerate(owner) if r == rank]
         for i in mine:
             a, B = mats[i]
-            cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*a), km, kn)
+            mk = pick_m(i, a)
+            cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*a), mk, kn)
             plan = sc.SpMMPlan(cf, N, device=local)
-            jobs.append({"plan": plan, "B": torch.from_numpy(B).to(dev), "rows": a[0], "max_rows": a[0],
+            jobs.append({"km": mk, "plan": plan, "B": torch.from_numpy(B).to(dev), "rows": a[0], "max_rows": a[0],
                          "m": a[0], "nnz_local": len(a[3]), "Bhost": B, "cuts": None, "K": a[1],
                          "C": torch.empty((a[0], N), device=dev)})
     else:
-        for a, B in mats:
+        for i, (a, B) in enumerate(mats):
             m = a[0]
-            cuts = balanced_panel_cuts(a[2], m, km, world)
+            mk = pick_m(i, a)
+            cuts = balanced_panel_cuts(a[2], m, mk, world)
             p0, p1 = cuts[rank], cuts[rank + 1]
-            r0, r1 = min(p0 * km, m), min(p1 * km, m)
+            r0, r1 = min(p0 * mk, m), min(p1 * mk, m)
             blk = row_slice(a, r0, r1)
-            cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*blk), km, kn)
+            cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*blk), mk, kn)
             plan = sc.SpMMPlan(cf, N, device=local)
-            max_rows = max(min(cuts[r + 1] * km, m) - min(cuts[r] * km, m) for r in range(world))
-            j = {"plan": plan, "B": torch.from_numpy(B).to(dev), "rows": r1 - r0, "max_rows": max_rows,
+            max_rows = max(min(cuts[r + 1] * mk, m) - min(cuts[r] * mk, m) for r in range(world))
+            j = {"km": mk, "plan": plan, "B": torch.from_numpy(B).to(dev), "rows": r1 - r0, "max_rows": max_rows,
                  "m": m, "nnz_local": len(blk[3]), "Bhost": B, "cuts": cuts, "K": a[1]}
             if world > 1 and args.exchange == "peer":
                 full, hdl = symmetric_buffer((m, N), dev)
@@ -409,17 +424,22 @@ def main():
                 j["gather"] = torch.empty((world, max_rows, N), device=dev)
                 j["C"] = j["gather"][rank, : j["rows"]] if world > 1 else torch.empty((j["rows"], N), device=dev)
             jobs.append(j)
-    batch = None
+    # one batched launch per kernel_m group of wide-B plans
+    batches = []
     if len(jobs) > 1 and jobs[0]["plan"].info["kernel"] == 2:
-        batch = sc.SpMMBatch([j["plan"] for j in jobs])
-        batch.bind([j["B"] for j in jobs], [j["C"] for j in jobs])
+        for mk in sorted({j["km"] for j in jobs}):
+            grp = [j for j in jobs if j["km"] == mk]
+            bt = sc.SpMMBatch([j["plan"] for j in grp])
+            bt.bind([j["B"] for j in grp], [j["C"] for j in grp])
+            batches.append(bt)
     t_setup = time.perf_counter() - t_setup
 
     peer_mode = world > 1 and not layers and args.exchange == "peer"
 
     def launch_all(stream):
-        if batch is not None:
-            batch.spmm(stream=stream)  # every local matrix in one kernel launch
+        if batches:
+            for bt in batches:
+                bt.spmm(stream=stream)  # every local matrix of one kernel_m in one kernel launch
         else:
             for j in jobs:
                 if peer_mode:  # the kernel stores each C tile locally and into every peer's C
@@ -506,8 +526,8 @@ def main():
                 elif rank == 0:
                     for j, hC in zip(jobs, hCs):
                         for r in range(world):
-                            a0 = min(j["cuts"][r] * km, j["m"])
-                            a1 = min(j["cuts"][r + 1] * km, j["m"])
+                            a0 = min(j["cuts"][r] * j["km"], j["m"])
+                            a1 = min(j["cuts"][r + 1] * j["km"], j["m"])
                             src = j["gather"][r, : a1 - a0] if world > 1 else j["C"]
                             hC[a0:a1].copy_(src, non_blocking=True)
                 torch.cuda.synchronize()
@@ -555,14 +575,18 @@ def main():
         "metric": "SpMM GFLOP/s (2*nnz*N)", "value": value, "unit": "GFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": name, "coarsening": [km, kn], "n_cols_b": N, "nnz": total_nnz,
+        "config": {"workload": name,
+                   "coarsening": ([km, kn] if not auto_m else
+                                  {"kernel_m": "auto (measured per matrix)", "chosen": sorted({j["km"] for j in jobs}),
+                                   "kernel_n": kn}),
+                   "n_cols_b": N, "nnz": total_nnz,
                    "parallelism": ("1 GPU" if world == 1 else
                                    f"whole matrices sharded over {world} GPUs (LPT by nnz), no collective"
                                    if layers else
                                    (f"row-partition x{world}; SpMM kernel stores C tiles into every peer over "
                                     "NVLink (symmetric memory) + one barrier" if peer_mode else
                                     f"row-partition x{world} + NCCL all-gather of C")),
-                   "launches_per_step": 1 if batch is not None else len(jobs),
+                   "launches_per_step": len(batches) if batches else len(jobs),
                    "l2": "flushed before every timed step (256 MiB write, outside the events)",
                    "plan": {k: info[k] for k in ("entries", "items", "kernel", "warps_per_panel",
                                                  "device_bytes")}},
@@ -575,7 +599,7 @@ def main():
                      "fp32_frac": local_flops / (kern_ms * 1e-3) / 1e12 / fp32_peak},
         "e2e": {"value": e2e_value, "unit": "GFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_s * 1e3},
-        "gpu_launches": args.steps * (1 if batch is not None else len(jobs)),
+        "gpu_launches": args.steps * (len(batches) if batches else len(jobs)),
         "clocks": clk,
         "setup_s": t_setup,
     }

@@ -267,3 +267,10 @@ def test_peer_store_epilogue_single_gpu(cuda):
     assert_parity(C.cpu().numpy(), a, B, rows=rows)
     with pytest.raises(sc.ScError):
         sc.SpMMPlan(cf, 4).spmm_peers(torch.zeros((512, 4), device=cuda), torch.zeros((2048, 4), device=cuda), peers)
+
+
+def test_autotune_kernel_m(cuda):
+    from sparse_computation_b200 import tuning
+    a, B = wl.config3((2048, 512), 128)
+    best, times = tuning.autotune_kernel_m(to_csr_handle(a), 128, candidates=(1, 4), reps=3)
+    assert best in (1, 4) and set(times) == {1, 4} and all(t > 0 for t in times.values())
