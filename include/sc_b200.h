@@ -82,6 +82,13 @@ int sc_cf_from_csr(const sc_csr *a, int32_t kernel_m, int32_t kernel_n,
  * (format_generator.py:132-160) for a CF built by sc_cf_from_csr; a CF read
  * by sc_cf_load is written back token for token. */
 int sc_cf_write(const sc_cf *cf, const char *path);
+/* Binary sidecar of a CF (".cfbin"): the same arrays as raw little-endian
+ * data on 16-byte boundaries, for large matrices whose text .cfmtx takes
+ * seconds to parse.  No reference counterpart (the reference reads only the
+ * text format, utils/Sparse_io.cpp:84-181); a CF loaded from a .cfbin writes
+ * back to the same .cfmtx text. */
+int sc_cf_write_binary(const sc_cf *cf, const char *path);
+int sc_cf_load_binary(const char *path, sc_cf **out);
 int sc_cf_dims(const sc_cf *cf, int32_t *num_rows, int32_t *num_cols,
                int32_t *kernel_m, int32_t *num_patterns, int32_t *vector_length);
 /* Header line i (0-based, file order): mask string (NUL-terminated, written

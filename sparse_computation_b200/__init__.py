@@ -47,7 +47,7 @@ EXPORTED_SYMBOLS = (
     "sc_mtx_load_csr", "sc_csr_create", "sc_csr_dims", "sc_csr_arrays", "sc_csr_free",
     "sc_cf_load", "sc_cf_from_csr", "sc_cf_write", "sc_cf_dims", "sc_cf_header_line",
     "sc_cf_pattern_sizes", "sc_cf_pattern_arrays", "sc_cf_real_nnz", "sc_cf_free",
-    "sc_companion_mtx_path",
+    "sc_companion_mtx_path", "sc_cf_write_binary", "sc_cf_load_binary",
     "sc_plan_create", "sc_plan_create_panels", "sc_plan_get_info", "sc_spmm", "sc_spmv",
     "sc_spmm_host", "sc_plan_free", "sc_spmm_peers",
     "sc_batch_create", "sc_batch_bind", "sc_batch_spmm", "sc_batch_free",
@@ -101,6 +101,8 @@ def lib() -> ctypes.CDLL:
         "sc_cf_real_nnz": ([vp, P(i64)], ctypes.c_int),
         "sc_cf_free": ([vp], None),
         "sc_companion_mtx_path": ([cp, ctypes.c_char_p, i32], ctypes.c_int),
+        "sc_cf_write_binary": ([vp, cp], ctypes.c_int),
+        "sc_cf_load_binary": ([cp, P(vp)], ctypes.c_int),
         "sc_plan_create": ([vp, i32, i32, P(vp)], ctypes.c_int),
         "sc_plan_create_panels": ([vp, i32, i32, i64, i64, P(vp)], ctypes.c_int),
         "sc_plan_get_info": ([vp, P(_PlanInfo)], ctypes.c_int),
@@ -260,6 +262,10 @@ class CompressedFormat:
     def write(self, path) -> None:
         _check(lib().sc_cf_write(self._h, _enc(path)))
 
+    def write_binary(self, path) -> None:
+        """Binary sidecar (.cfbin): fast to load, same content."""
+        _check(lib().sc_cf_write_binary(self._h, _enc(path)))
+
     def __del__(self):
         if getattr(self, "_h", None) and self._h.value and _lib is not None:
             _lib.sc_cf_free(self._h)
@@ -288,6 +294,13 @@ def read_cfmtx(path) -> CompressedFormat:
     """Parses a .cfmtx (readCFMTXFile, utils/Sparse_io.cpp:84-181)."""
     h = ctypes.c_void_p()
     _check(lib().sc_cf_load(_enc(path), ctypes.byref(h)))
+    return CompressedFormat(h.value)
+
+
+def read_cfbin(path) -> CompressedFormat:
+    """Loads a binary sidecar written by CompressedFormat.write_binary."""
+    h = ctypes.c_void_p()
+    _check(lib().sc_cf_load_binary(_enc(path), ctypes.byref(h)))
     return CompressedFormat(h.value)
 
 

@@ -6,6 +6,7 @@
 // native code, one row panel per task, with panels spread over host threads.
 
 #include <algorithm>
+#include <charconv>
 #include <cerrno>
 #include <cinttypes>
 #include <cmath>
@@ -62,12 +63,11 @@ std::string sc_py_float_repr(double d) {
   if (std::isnan(d)) return "nan";
   if (std::isinf(d)) return d < 0 ? "-inf" : "inf";
   if (d == 0.0) return std::signbit(d) ? "-0.0" : "0.0";
+  // Shortest round-trip digits in scientific form (std::to_chars, i.e. the
+  // Ryu algorithm in libstdc++), then Python's layout below.
   char buf[64];
-  int prec = 1;
-  for (; prec <= 17; ++prec) {
-    snprintf(buf, sizeof buf, "%.*e", prec - 1, d);
-    if (strtod(buf, nullptr) == d) break;
-  }
+  auto res = std::to_chars(buf, buf + sizeof buf - 1, d, std::chars_format::scientific);
+  *res.ptr = '\0';
   // buf = [-]D[.DDD]e[+-]XX
   std::string s(buf);
   bool neg = s[0] == '-';
@@ -397,6 +397,110 @@ static void write_cfmtx(const sc_cf *cf, const char *path) {
   flush();
   bool err = fclose(f) != 0;
   require(!err, SC_ERR_IO, std::string("close error on ") + path);
+}
+
+// ------------------------------------------------------ binary sidecar ----
+
+// Binary companion of a .cfmtx ("<file>.cfbin"): the same content as raw
+// little-endian arrays, every array starting on a 16-byte boundary, so
+// loading is a few large reads instead of parsing ~10 text tokens per
+// nonzero.  Layout:
+//   "SCCFBIN1" | i32 num_rows, num_cols, kernel_m, num_patterns, vector_length,
+//   i32 0 | i64 real_nnz | per header line: i32 id, i32 len, mask bytes |
+//   per pattern (pad to 16): i32 popcount, i32 mask_len, i64 n_rpp, n_cb, n_vals,
+//   mask bytes, then (each padded to 16) rpp i32[], cb i32[], vals f32[],
+//   vals_d f64[], pad u8[].
+static const char kBinMagic[8] = {'S', 'C', 'C', 'F', 'B', 'I', 'N', '1'};
+
+static void write_cfbin(const sc_cf *cf, const char *path) {
+  require(path != nullptr, SC_ERR_ARG, "null path");
+  FILE *f = fopen(path, "wb");
+  require(f != nullptr, SC_ERR_IO, std::string("unable to open file for writing ") + path);
+  size_t pos = 0;
+  bool ok = true;
+  auto put = [&](const void *p, size_t n) {
+    if (n && fwrite(p, 1, n, f) != n) ok = false;
+    pos += n;
+  };
+  auto align16 = [&]() {
+    static const char z[16] = {0};
+    if (pos % 16) put(z, 16 - pos % 16);
+  };
+  put(kBinMagic, 8);
+  int32_t h[6] = {cf->num_rows, cf->num_cols, cf->kernel_m, (int32_t)cf->header.size(), cf->vector_length_hdr, 0};
+  put(h, sizeof h);
+  put(&cf->real_nnz, 8);
+  for (auto &l : cf->header) {
+    int32_t x[2] = {l.second, (int32_t)l.first.size()};
+    put(x, 8);
+    put(l.first.data(), l.first.size());
+  }
+  for (auto &pt : cf->pats) {
+    align16();
+    int32_t a[2] = {pt.popcount, (int32_t)pt.mask.size()};
+    int64_t b[3] = {(int64_t)pt.rpp.size(), (int64_t)pt.cb.size(), (int64_t)pt.vals.size()};
+    put(a, 8);
+    put(b, 24);
+    put(pt.mask.data(), pt.mask.size());
+    align16(); put(pt.rpp.data(), pt.rpp.size() * 4);
+    align16(); put(pt.cb.data(), pt.cb.size() * 4);
+    align16(); put(pt.vals.data(), pt.vals.size() * 4);
+    align16(); put(pt.vals_d.data(), pt.vals_d.size() * 8);
+    align16(); put(pt.pad.data(), pt.pad.size());
+  }
+  ok = (fclose(f) == 0) && ok;
+  require(ok, SC_ERR_IO, std::string("write error on ") + path);
+}
+
+static sc_cf *load_cfbin(const char *path) {
+  std::string d = read_file(path);
+  size_t pos = 0;
+  auto get = [&](void *p, size_t n) {
+    require(pos + n <= d.size(), SC_ERR_FORMAT, "truncated .cfbin file");
+    if (n) memcpy(p, d.data() + pos, n);
+    pos += n;
+  };
+  auto align16 = [&]() { pos = (pos + 15) & ~(size_t)15; };
+  char magic[8];
+  get(magic, 8);
+  require(memcmp(magic, kBinMagic, 8) == 0, SC_ERR_FORMAT, "not a .cfbin file (bad magic)");
+  auto *cf = new sc_cf();
+  std::unique_ptr<sc_cf> guard(cf);
+  int32_t h[6];
+  get(h, sizeof h);
+  cf->num_rows = h[0]; cf->num_cols = h[1]; cf->kernel_m = h[2]; cf->vector_length_hdr = h[4];
+  require(h[3] >= 0 && h[0] >= 0 && h[1] >= 0 && h[2] >= 1, SC_ERR_FORMAT, "bad .cfbin header");
+  get(&cf->real_nnz, 8);
+  cf->header.resize(h[3]);
+  cf->pats.resize(h[3]);
+  for (auto &l : cf->header) {
+    int32_t x[2];
+    get(x, 8);
+    require(x[1] >= 0 && x[1] < 4096, SC_ERR_FORMAT, "bad mask length in .cfbin");
+    l.second = x[0];
+    l.first.assign((size_t)x[1], '0');
+    get(&l.first[0], (size_t)x[1]);
+  }
+  for (auto &pt : cf->pats) {
+    align16();
+    int32_t a[2];
+    int64_t b[3];
+    get(a, 8);
+    get(b, 24);
+    require(a[1] >= 0 && a[1] < 4096 && b[0] >= 0 && b[1] >= 0 && b[2] >= 0 &&
+                (size_t)(b[0] + b[1] + b[2]) <= d.size(),
+            SC_ERR_FORMAT, "bad pattern sizes in .cfbin");
+    pt.popcount = a[0];
+    pt.mask.assign((size_t)a[1], '0');
+    get(&pt.mask[0], (size_t)a[1]);
+    pt.rpp.resize(b[0]); pt.cb.resize(b[1]); pt.vals.resize(b[2]); pt.vals_d.resize(b[2]); pt.pad.resize(b[2]);
+    align16(); get(pt.rpp.data(), b[0] * 4);
+    align16(); get(pt.cb.data(), b[1] * 4);
+    align16(); get(pt.vals.data(), b[2] * 4);
+    align16(); get(pt.vals_d.data(), b[2] * 8);
+    align16(); get(pt.pad.data(), b[2]);
+  }
+  return guard.release();
 }
 
 // ----------------------------------------------------- pattern dictionary --
@@ -733,6 +837,20 @@ int sc_cf_write(const sc_cf *cf, const char *path) {
   SC_API_BEGIN
   require(cf != nullptr, SC_ERR_ARG, "null CF handle");
   write_cfmtx(cf, path);
+  SC_API_END
+}
+
+int sc_cf_write_binary(const sc_cf *cf, const char *path) {
+  SC_API_BEGIN
+  require(cf != nullptr, SC_ERR_ARG, "null CF handle");
+  write_cfbin(cf, path);
+  SC_API_END
+}
+
+int sc_cf_load_binary(const char *path, sc_cf **out) {
+  SC_API_BEGIN
+  require(out != nullptr, SC_ERR_ARG, "null output handle");
+  *out = load_cfbin(path);
   SC_API_END
 }
 

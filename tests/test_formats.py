@@ -183,3 +183,31 @@ def test_float_repr_matches_python(tmp_path):
     cf.write(tmp_path / "v.cfmtx")
     line = open(tmp_path / "v.cfmtx").read().split("\n")[4]
     assert line.split(" ") == [str(np.float64(v)) for v in vals]
+
+
+def test_binary_sidecar_roundtrip(tmp_path):
+    for f, *_ in golden_cases():
+        cf = sc.read_cfmtx(f)
+        cf.write_binary(tmp_path / "x.cfbin")
+        cb = sc.read_cfbin(tmp_path / "x.cfbin")
+        assert cb.header == cf.header and cb.num_patterns == cf.num_patterns and cb.real_nnz == cf.real_nnz
+        for pid in range(cf.num_patterns):
+            a, b = cf.pattern(pid), cb.pattern(pid)
+            assert a[0] == b[0] and all(np.array_equal(x, y) for x, y in zip(a[1:], b[1:]))
+        cb.write(tmp_path / "back.cfmtx")
+        assert open(tmp_path / "back.cfmtx").read() == open(f).read()
+    # from a CF built in memory
+    a = wl.config3((512, 2048), 32)[0]
+    cf = sc.csr_to_compressed_format_converter(_py_csr(a), 5, 3)
+    cf.write(tmp_path / "m.cfmtx")
+    cf.write_binary(tmp_path / "m.cfbin")
+    sc.read_cfbin(tmp_path / "m.cfbin").write(tmp_path / "m2.cfmtx")
+    assert open(tmp_path / "m2.cfmtx").read() == open(tmp_path / "m.cfmtx").read()
+    # corrupt / truncated
+    data = open(tmp_path / "m.cfbin", "rb").read()
+    open(tmp_path / "t.cfbin", "wb").write(data[: len(data) // 2])
+    with pytest.raises(sc.ScError) as e:
+        sc.read_cfbin(tmp_path / "t.cfbin")
+    assert e.value.code == sc.SC_ERR_FORMAT
+    with pytest.raises(sc.ScError):
+        sc.read_cfbin(tmp_path / "m.cfmtx")
