@@ -107,29 +107,67 @@ def symmetric_buffer(shape, dev):
 # ---------------------------------------------------------------- clocks --
 
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons every 200 ms."""
+    """Samples the SM clock and clock-event (throttle) reasons of the bench's
+    GPU through NVML (read-only queries) every 5 ms; only samples taken while
+    `timed` is set are summarised, so the record covers the timed region.
+    Falls back to `nvidia-smi` polling when NVML is unavailable."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+               "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+               "sw_power_cap": "nvmlClocksEventReasonSwPowerCap"}
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.rows = []
+    def __init__(self, cuda_index: int):
+        self.rows = []  # (sm_mhz, max_mhz, [reasons])
+        self.timed = False
         self._stop = threading.Event()
+        self._h = None
+        self._nv = None
+        try:
+            import pynvml as nv
+            import torch
+            nv.nvmlInit()
+            props = torch.cuda.get_device_properties(cuda_index)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            self._h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            self._nv = nv
+        except Exception:
+            self._h = None
+        self.idx = cuda_index
         self._t = threading.Thread(target=self._run, daemon=True)
 
+    def _sample(self):
+        if self._h is not None:
+            nv = self._nv
+            sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+            mx = nv.nvmlDeviceGetMaxClockInfo(self._h, nv.NVML_CLOCK_SM)
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            rs = [k for k, attr in self.REASONS.items() if bits & getattr(nv, attr)]
+            return float(sm), float(mx), rs
+        out = subprocess.run(["nvidia-smi", "-i", str(self.idx), "--query-gpu=clocks.sm,clocks.max.sm,"
+                              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                              "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5).stdout
+        f = [x.strip() for x in out.strip().split(",")]
+        rs = [k for k, v in zip(self.REASONS, f[2:]) if v == "Active"]
+        return float(f[0]), float(f[1]), rs
+
+    def sample_now(self):
+        """One synchronous sample (call while the GPU is busy with timed work)."""
+        try:
+            self.rows.append(self._sample())
+        except Exception:
+            pass
+
     def _run(self):
+        period = 0.005 if self._h is not None else 0.2
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                     timeout=5).stdout.strip()
-                if out:
-                    self.rows.append([x.strip() for x in out.split(",")])
+                if self.timed:
+                    self.rows.append(self._sample())
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(period)
 
     def __enter__(self):
         self._t.start()
@@ -141,13 +179,15 @@ class ClockSampler:
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+            try:
+                self.rows.append(self._sample())
+            except Exception:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock query unavailable"], "samples": 0}
+        sm = [r[0] for r in self.rows]
+        reasons = sorted({x for r in self.rows for x in r[2]})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(r[1] for r in self.rows), "reasons": reasons,
+                "samples": len(self.rows), "source": "nvml" if self._h is not None else "nvidia-smi",
+                "window": "timed region"}
 
 
 def measured_peak_hbm():
@@ -473,6 +513,7 @@ def main():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        clocks.timed = True
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         kstarts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -485,10 +526,12 @@ def main():
             kends[i].record(stream)
             gather_all()
             ends[i].record(stream)
+        clocks.sample_now()  # the GPU is still working through the timed steps
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        clocks.timed = False
         step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
         kern_ms = sum(s.elapsed_time(e) for s, e in zip(kstarts, kends)) / args.steps
 

@@ -67,6 +67,24 @@ __device__ __forceinline__ void load_vec(const float *p, float (&out)[VEC]) {
   }
 }
 
+// B-row loads of the wide kernel: read-only, and (SC_B_NOALLOC) without
+// allocating in L1 -- a B row is rarely re-read by the same SM before eviction.
+template <int VEC>
+__device__ __forceinline__ void load_b(const float *p, float (&out)[VEC]) {
+#if SC_B_NOALLOC
+  if constexpr (VEC == 1) {
+    asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(out[0]) : "l"(p));
+  } else if constexpr (VEC == 2) {
+    asm volatile("ld.global.nc.L1::no_allocate.v2.f32 {%0,%1}, [%2];" : "=f"(out[0]), "=f"(out[1]) : "l"(p));
+  } else {
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(out[0]), "=f"(out[1]), "=f"(out[2]), "=f"(out[3]) : "l"(p));
+  }
+#else
+  load_vec<VEC>(p, out);
+#endif
+}
+
 // Loads one record (column + P values) at `r`.
 template <int P>
 __device__ __forceinline__ void load_rec(const uint32_t *__restrict__ r, int &col, float (&v)[P]) {
@@ -121,6 +139,9 @@ struct WideArgs {
   float *peers[kMaxPeers];
 };
 
+#ifndef SC_B_NOALLOC
+#define SC_B_NOALLOC 0
+#endif
 #ifndef SC_WIDE_U
 #define SC_WIDE_U 8
 #endif
@@ -183,7 +204,7 @@ __device__ __forceinline__ void seg_wide(const uint32_t *rbuf, int len, const ch
       uint32_t col;
       lds_rec<P>(rbuf + min(e0 + u, len - 1) * S, col, v[u]);
       if (active && e0 + u < len) {
-        load_vec<VEC>(reinterpret_cast<const float *>(Bcol + (uint64_t)col * ldb_bytes), b[u]);
+        load_b<VEC>(reinterpret_cast<const float *>(Bcol + (uint64_t)col * ldb_bytes), b[u]);
       } else {
 #pragma unroll
         for (int q = 0; q < VEC; ++q) b[u][q] = 0.f;

@@ -10,6 +10,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -74,7 +75,32 @@ namespace {
 using sc::WideFn;
 using sc::NarrowFn;
 
-WideFn wide_kernel(int km, int vec, bool batch) {
+// Shared-memory carveout preference (percent) applied once per kernel;
+// SC_CARVEOUT overrides for tuning experiments (-1 = driver default).
+int carveout_percent() {
+  static const int v = [] {
+    const char *e = getenv("SC_CARVEOUT");
+    return e ? atoi(e) : -1;
+  }();
+  return v;
+}
+
+template <typename F>
+F with_carveout(F fn) {
+  static std::mutex mu;
+  static std::vector<const void *> done;
+  const int pct = carveout_percent();
+  if (pct < 0) return fn;
+  std::lock_guard<std::mutex> g(mu);
+  const void *key = reinterpret_cast<const void *>(fn);
+  if (std::find(done.begin(), done.end(), key) == done.end()) {
+    cudaFuncSetAttribute(key, cudaFuncAttributePreferredSharedMemoryCarveout, pct);
+    done.push_back(key);
+  }
+  return fn;
+}
+
+WideFn wide_kernel_raw(int km, int vec, bool batch) {
   switch (km) {
     case 1: return sc_wide_kernel_km1(vec, batch);
     case 2: return sc_wide_kernel_km2(vec, batch);
@@ -84,6 +110,7 @@ WideFn wide_kernel(int km, int vec, bool batch) {
     default: return sc_wide_kernel_km6(vec, batch);
   }
 }
+WideFn wide_kernel(int km, int vec, bool batch) { return with_carveout(wide_kernel_raw(km, vec, batch)); }
 
 NarrowFn narrow_kernel(int km, int nb) {
   switch (km) {
