@@ -89,3 +89,41 @@ def test_companion_path():
     assert sc.companion_mtx_path("mat-4.cfmtx") == "mat-4.mtx"
     assert sc.companion_mtx_path("-4.cfmtx") == "-4.mtx"
     assert sc.companion_mtx_path(".cfmtx") == ".cfmtx"
+
+
+def _cf_text(rpp_line="0 1 1", cb_line="2", vals_line="1.5"):
+    # 4x4 matrix, kernel_m 2, one pattern "11"... plus the other two patterns empty
+    return ("4 4 2 3 1\n11 0 \n10 1 \n01 2 \n"
+            f"{rpp_line}\n{cb_line}\n{' '.join([vals_line, vals_line])}\n"
+            "0 0 0\n\n\n0 0 0\n\n\n")
+
+
+@pytest.mark.parametrize("text,what", [
+    (_cf_text(cb_line="9"), "column index out of range"),
+    (_cf_text(rpp_line="0 1"), "row-panel pointer length"),
+    (_cf_text(rpp_line="1 1 1"), "must start at 0"),
+    (_cf_text(rpp_line="0 2 1", cb_line="1 2"), "non-decreasing"),
+    (_cf_text(rpp_line="0 1 3", cb_line="1 2"), "exceeds column list"),
+    (_cf_text(vals_line="1.5").replace("1.5 1.5", "1.5"), "shorter than columns"),
+])
+def test_plan_validates_cf_on_host(tmp_path, text, what):
+    """Corrupt .cfmtx content is rejected before anything reaches a GPU
+    (SC_ERR_FORMAT), whether or not a GPU is present."""
+    f = tmp_path / "bad-2-1.cfmtx"
+    f.write_text(text)
+    cf = sc.read_cfmtx(f)  # the loader is as lenient as the reference's
+    with pytest.raises(sc.ScError) as e:
+        sc.SpMMPlan(cf, 32)
+    assert e.value.code == sc.SC_ERR_FORMAT and what in str(e.value)
+
+
+def test_valid_small_cf_reaches_device_step(tmp_path):
+    f = tmp_path / "ok-2-1.cfmtx"
+    f.write_text(_cf_text())
+    cf = sc.read_cfmtx(f)
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present: covered by the GPU tests")
+    with pytest.raises(sc.ScError) as e:
+        sc.SpMMPlan(cf, 32)
+    assert e.value.code == sc.SC_ERR_CUDA
