@@ -466,7 +466,7 @@ def main():
             jobs.append(j)
     # one batched launch per kernel_m group of wide-B plans
     batches = []
-    if len(jobs) > 1 and jobs[0]["plan"].info["kernel"] == 2:
+    if len(jobs) > 1 and jobs[0]["plan"].info["kernel"] in (2, 3):
         for mk in sorted({j["km"] for j in jobs}):
             grp = [j for j in jobs if j["km"] == mk]
             bt = sc.SpMMBatch([j["plan"] for j in grp])

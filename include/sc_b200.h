@@ -132,7 +132,8 @@ typedef struct sc_plan_info {
   int64_t entries;       /* (panel, column) entries after dropping padding */
   int64_t items;         /* scheduled work items */
   int64_t device_bytes;  /* device memory held by the plan */
-  int32_t kernel;        /* 1 = small-B (N<=4) kernel, 2 = large-B kernel */
+  int32_t kernel;        /* 1 = small-B (N<=4) kernel, 2 = large-B kernel,
+                            3 = dense-tile tensor-core (tcgen05 3xTF32) kernel */
   int32_t warps_per_panel;
 } sc_plan_info;
 int sc_plan_get_info(const sc_plan *p, sc_plan_info *info);

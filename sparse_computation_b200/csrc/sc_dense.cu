@@ -1,0 +1,369 @@
+// Dense-tile tcgen05 kernels (see sc_dense.cuh for the scheme).
+//
+// CTA = one 128-row block x one 128-column C tile, 4 warps:
+//   thread 0   producer: per kept K-chunk, bulk-copies the A_hi, A_lo, B_hi,
+//              B_lo tile images (4 x 16 KiB) into a 3-stage ring, completion
+//              tracked by mbarrier transaction counts;
+//   thread 32  MMA issuer: per stage 4 k-steps x 3 tcgen05.mma (kind::tf32,
+//              M=128, N=128, K=8) into one 128x128 fp32 accumulator in tensor
+//              memory; tcgen05.commit releases the stage back to the producer;
+//   all warps  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes
+//              32w..32w+31 = C rows), then row-contiguous stores of C.
+// Every wait on an mbarrier is bounded; on expiry the CTA records an error in
+// *status, stops issuing work, and still releases its tensor memory.
+#include <cstring>
+
+#include <cooperative_groups.h>
+
+#include "sc_dense.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace sc {
+namespace dense {
+namespace {
+
+constexpr uint32_t kWaitLimit = 1u << 18;  // polls of mbarrier.try_wait (each suspends briefly)
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; false when the limit expired.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (abort_flag && *abort_flag) return false;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void bulk_copy(void *dst_smem, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// tcgen05 shared-memory matrix descriptor: K-major, 128B swizzle, 8-row
+// groups 1024 bytes apart (tile base 1024-byte aligned).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address       [0,14)
+  d |= (uint64_t)1 << 16;                     // leading byte offset [16,30) (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;           // stride byte offset  [32,46)
+  d |= (uint64_t)1 << 46;                     // descriptor version  [46,48)
+  d |= (uint64_t)2 << 61;                     // SWIZZLE_128B        [61,64)
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, both K-major, N=128, M=128.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                            ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accum)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 consecutive accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Sum of the partial accumulators of a cluster of S CTAs (split K): warp w's
+// TMEM rows (C rows 32w..32w+31 of the tile) are owned by CTA w / (4/S); the
+// other CTAs send theirs into the owner's shared memory (slots of 32 rows x
+// 128 floats), then the owner adds them up and stores C.
+template <bool BATCH>
+__global__ void __launch_bounds__(kThreads, 1)
+dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *__restrict__ tasks, int accumulate,
+                  int *status) {
+  extern __shared__ __align__(1024) uint8_t dsmem[];
+  // 1024-byte aligned stage ring (the swizzle is applied on address bits).
+  uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages], done_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = (int)cluster.num_blocks();
+  const int crank = (int)cluster.block_rank();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int4 task = tasks[blockIdx.x / S];
+  DenseMat m;
+  if constexpr (BATCH) m = mats[task.x];
+  else m = one;
+  const int rb = task.y, nt = task.z;
+  const int c0 = m.rb_ptr[rb], c1 = m.rb_ptr[rb + 1];
+  // this CTA's kept chunks: c0 + crank, c0 + crank + S, ...
+  const int nk = (c1 - c0 > crank) ? (c1 - c0 - crank + S - 1) / S : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&done_bar, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(kBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (threadIdx.x == 0 && nk > 0) {
+    // producer
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % kStages;
+      if (i >= kStages && !mbar_wait(&empty_bar[s], ((i / kStages) - 1) & 1, &abort_flag)) {
+        atomicExch(status, 1);
+        abort_flag = 1;
+        break;
+      }
+      const int ci = c0 + crank + i * S;
+      uint8_t *st = ring + (size_t)s * kStageBytes;
+      const uint8_t *at = m.a_tiles + (size_t)ci * 2 * kTileBytes;
+      const int kc = m.rb_chunk[ci];
+      const uint8_t *bt = m.b_tiles + ((size_t)nt * m.k_chunks + kc) * 2 * kTileBytes;
+      mbar_expect_tx(&full_bar[s], kStageBytes);
+      bulk_copy(st, at, 2 * kTileBytes, &full_bar[s]);
+      bulk_copy(st + 2 * kTileBytes, bt, 2 * kTileBytes, &full_bar[s]);
+    }
+  } else if (threadIdx.x == 32 && nk > 0) {
+    // MMA issuer
+    bool ok = true;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % kStages;
+      if (!mbar_wait(&full_bar[s], (i / kStages) & 1, &abort_flag)) {
+        atomicExch(status, 2);
+        abort_flag = 1;
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t base = smem_u32(ring + (size_t)s * kStageBytes);
+      const uint64_t a_hi = sdesc(base), a_lo = sdesc(base + kTileBytes);
+      const uint64_t b_hi = sdesc(base + 2 * kTileBytes), b_lo = sdesc(base + 3 * kTileBytes);
+#pragma unroll
+      for (int k = 0; k < kBK / 8; ++k) {
+        const uint64_t step = (uint64_t)((k * 32) >> 4);  // 8 tf32 = 32 bytes along K
+        mma_tf32(tmem, a_lo + step, b_hi + step, (i > 0 || k > 0) ? 1u : 0u);
+        mma_tf32(tmem, a_hi + step, b_lo + step, 1u);
+        mma_tf32(tmem, a_hi + step, b_hi + step, 1u);
+      }
+      mma_commit(&empty_bar[s]);  // stage free once these MMAs have read it
+    }
+    if (ok) mma_commit(&done_bar);
+    else abort_flag = 1;
+  }
+
+  // ---- epilogue
+  bool have = nk > 0;
+  if (have && !mbar_wait(&done_bar, 0, &abort_flag)) {
+    if (lane == 0) atomicExch(status, 3);
+    abort_flag = 1;
+    have = false;
+  }
+  __syncwarp();
+  tc_fence_after();
+  const int64_t row = (int64_t)rb * kBM + warp * 32 + lane;
+  const int col_base = nt * kBN;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  const int wpc = 4 / S;           // warps (row groups) owned per CTA
+  const int owner = warp / wpc;    // CTA that finalises this warp's rows
+  constexpr int kSlotFloats = 32 * kBN;
+  if (S > 1) {
+    cluster.sync();  // every CTA's MMAs are done: stage rings are free
+    if (owner != crank) {
+      const int sidx = crank < owner ? crank : crank - 1;
+      float *slot = reinterpret_cast<float *>(ring) + ((warp - owner * wpc) * (S - 1) + sidx) * kSlotFloats;
+      float *dst = cluster.map_shared_rank(slot, owner) + lane * kBN;
+#pragma unroll 1
+      for (int cb = 0; cb < kBN / 32; ++cb) {
+        float v[32];
+        if (have) tmem_ld32(trow + (uint32_t)(cb * 32), v);
+        else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4 *>(dst + cb * 32 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      }
+    }
+    cluster.sync();  // partials delivered
+  }
+  if (owner == crank) {
+#pragma unroll 1
+    for (int cb = 0; cb < kBN / 32; ++cb) {
+      float v[32];
+      if (have) tmem_ld32(trow + (uint32_t)(cb * 32), v);
+      else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      for (int sidx = 0; sidx < S - 1; ++sidx) {
+        const float *src = reinterpret_cast<const float *>(ring) +
+                           ((warp - owner * wpc) * (S - 1) + sidx) * kSlotFloats + lane * kBN + cb * 32;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 x = *reinterpret_cast<const float4 *>(src + i);
+          v[i] += x.x; v[i + 1] += x.y; v[i + 2] += x.z; v[i + 3] += x.w;
+        }
+      }
+      if (row < m.rows && !abort_flag) {
+        float *c = m.C + row * m.ldc + col_base + cb * 32;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          if (accumulate) {
+            const float4 x = *reinterpret_cast<const float4 *>(c + i);
+            o.x += x.x; o.y += x.y; o.z += x.z; o.w += x.w;
+          }
+          *reinterpret_cast<float4 *>(c + i) = o;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN));
+  }
+}
+
+// B (K x N row-major fp32) -> per (n tile, K chunk) [hi | lo] K-major
+// swizzled images; rows of a B image are C columns (n), K-chunk tail zeroed.
+// Block (x, y): tile x of matrix y.  The 32 x 128 chunk is read coalesced
+// (n fastest) into shared memory, then the images are written in order.
+template <bool BATCH>
+__global__ void __launch_bounds__(256) split_b_kernel(DenseMat one, const DenseMat *__restrict__ mats) {
+  __shared__ float T[kBK][kBN + 1];
+  DenseMat m;
+  if constexpr (BATCH) m = mats[blockIdx.y];
+  else m = one;
+  const int tile = blockIdx.x;
+  if (tile >= m.n_tiles * m.k_chunks) return;
+  const int nt = tile / m.k_chunks, kc = tile % m.k_chunks;
+  for (int e = threadIdx.x; e < kBN * kBK; e += blockDim.x) {
+    const int n = e % kBN, k = e / kBN;
+    const int gk = kc * kBK + k, gn = nt * kBN + n;
+    T[k][n] = (gk < m.k_rows && gn < m.n_cols) ? __ldg(m.B + (int64_t)gk * m.ldb + gn) : 0.f;
+  }
+  __syncthreads();
+  float4 *hi = reinterpret_cast<float4 *>(m.b_tiles + ((size_t)nt * m.k_chunks + kc) * 2 * kTileBytes);
+  float4 *lo = hi + kTileBytes / 16;
+  // 16-byte chunk q of the image: row n = q / 8, physical chunk c = q % 8,
+  // holding logical k = 4 * (c ^ (n & 7)) .. +3
+  for (int q = threadIdx.x; q < kBN * kBK / 4; q += blockDim.x) {
+    const int n = q >> 3, c = q & 7;
+    const int k0 = ((c ^ (n & 7)) << 2);
+    float h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float x = T[k0 + j][n];
+      h[j] = tf32_round(x);
+      l[j] = tf32_round(x - h[j]);
+    }
+    hi[q] = make_float4(h[0], h[1], h[2], h[3]);
+    lo[q] = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+}  // namespace
+}  // namespace dense
+}  // namespace sc
+
+int sc_dense_split_b(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, int nmats, int max_tiles,
+                     cudaStream_t s) {
+  using namespace sc::dense;
+  if (nmats <= 0 || max_tiles <= 0) return 0;
+  if (mats) split_b_kernel<true><<<dim3(max_tiles, nmats), 256, 0, s>>>(one, mats);
+  else split_b_kernel<false><<<dim3(max_tiles, 1), 256, 0, s>>>(one, nullptr);
+  return (int)cudaGetLastError();
+}
+
+int sc_dense_gemm(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, const int4 *tasks,
+                  int64_t ntasks, int split, int accumulate, int *status, cudaStream_t s) {
+  using namespace sc::dense;
+  if (ntasks <= 0) return 0;
+  const size_t smem = (size_t)kStages * kStageBytes + 1024;
+  auto fn = mats ? dense_gemm_kernel<true> : dense_gemm_kernel<false>;
+  static unsigned attr_done[2] = {0, 0};  // one bit per device ordinal (< 32)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  unsigned &bits = attr_done[mats ? 1 : 0];
+  if (dev >= 32 || !(bits & (1u << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 32) bits |= 1u << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(ntasks * split), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = split > 1 ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, one, mats, tasks, accumulate, status);
+  if (e != cudaSuccess) return (int)e;
+  return (int)cudaGetLastError();
+}

@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "sc_internal.h"
+#include "sc_dense.cuh"
 #include "sc_kernels.cuh"
 
 namespace {
@@ -57,12 +58,23 @@ struct sc_plan {
   const int32_t *order = nullptr;
   float *stage_b = nullptr, *stage_c = nullptr;
   std::vector<int64_t> work;  // per local panel, for batch scheduling
+  // Dense-tile tensor-core path (kernel == 3): swizzled A_hi/A_lo tiles of
+  // the kept (row block, K-chunk) pairs, per-call B tile images, error word.
+  uint8_t *a_tiles = nullptr;
+  int32_t *rb_ptr = nullptr, *rb_chunk = nullptr;
+  uint8_t *b_tiles = nullptr;
+  int *status = nullptr;
+  int64_t row_blocks = 0, kept_chunks = 0;
+  int4 *dense_tasks = nullptr;  // {0, row block, n tile, kept chunks}, heaviest first
+  int64_t dense_ntasks = 0;
+  int dense_split = 1;          // CTAs (cluster) per task
   ~sc_plan() {
-    if (dev || stage_b || stage_c) {
+    if (dev || stage_b || stage_c || a_tiles) {
       int prev;
       bool ok = cudaGetDevice(&prev) == cudaSuccess;
       if (ok && prev != device) cudaSetDevice(device);
       if (dev) cudaFree(dev);
+      if (a_tiles) cudaFree(a_tiles);  // one allocation: tiles | rb_ptr | rb_chunk | b_tiles | status
       if (stage_b) cudaFree(stage_b);
       if (stage_c) cudaFree(stage_c);
       if (ok && prev != device) cudaSetDevice(prev);
@@ -138,6 +150,139 @@ int64_t target_warps() {
     return (int64_t)(x > 0 ? x : 148 * 64);
   }();
   return v;
+}
+
+// ---- dense-tile tensor-core path selection and tile building
+
+// SC_DENSE=0 disables, =1 forces (when N is a multiple of 128); by default
+// the path is used where the dense tiles cost less than the sparse gather:
+// density >= 8% (measured crossover region) and a dense row block of A that
+// fits comfortably in memory.
+// CTAs per dense task (split K over a cluster) so that small matrices still
+// spread over the SMs, keeping >= 4 kept chunks per CTA.
+int dense_split_for(const std::vector<int4> &tasks) {
+  int64_t chunks = 0;
+  for (auto &t : tasks) chunks += t.w;
+  const int64_t nt = (int64_t)tasks.size();
+  if (nt == 0) return 1;
+  int sp = 1;
+  while (sp < sc::dense::kMaxSplit && nt * sp < 148 && chunks / (nt * sp * 2) >= 4) sp <<= 1;
+  return sp;
+}
+
+sc::dense::DenseMat dense_mat(const sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc) {
+  sc::dense::DenseMat m;
+  m.a_tiles = p->a_tiles;
+  m.rb_ptr = p->rb_ptr;
+  m.rb_chunk = p->rb_chunk;
+  m.b_tiles = p->b_tiles;
+  m.B = B;
+  m.ldb = ldb;
+  m.C = C;
+  m.ldc = ldc;
+  m.rows = p->rows;
+  m.k_rows = (int)p->cols;
+  m.n_cols = (int)p->n;
+  m.k_chunks = (int)((p->cols + sc::dense::kBK - 1) / sc::dense::kBK);
+  m.n_tiles = (int)(p->n / sc::dense::kBN);
+  return m;
+}
+
+bool use_dense(const sc_plan &p, const sc_cf &cf) {
+  const char *e = getenv("SC_DENSE");
+  if (e && e[0] == '0') return false;
+  if (p.n % sc::dense::kBN != 0) return false;
+  const double cells = (double)p.rows * (double)p.cols;
+  if (cells <= 0 || (double)p.rows * p.cols * 4.0 > 2e9) return false;
+  if (e && e[0] == '1') return true;
+  return (double)p.nnz / cells >= 0.08;
+}
+
+void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int> &rowbits) {
+  using namespace sc::dense;
+  const int km = (int)p.km;
+  const int64_t rows = p.rows, K = p.cols;
+  const int64_t rbs = (rows + kBM - 1) / kBM;
+  const int kcs = (int)((K + kBK - 1) / kBK);
+  // densify this plan's rows
+  std::vector<float> A((size_t)rbs * kBM * K, 0.f);
+  for (int64_t lp = 0; lp < p.panels; ++lp) {
+    const int64_t gp = pb + lp;
+    for (size_t g = 0; g < cf.pats.size(); ++g) {
+      const sc_pattern &pt = cf.pats[g];
+      const int P = pt.popcount;
+      int rowsof[32];
+      int n = 0;
+      for (int j = 0; j < km && n < 32; ++j)
+        if (rowbits[g] >> j & 1) rowsof[n++] = j;
+      for (int32_t j = pt.rpp[gp]; j < pt.rpp[gp + 1]; ++j)
+        for (int q = 0; q < P; ++q) {
+          if (pt.pad[(size_t)j * P + q]) continue;
+          const int64_t r = lp * km + rowsof[q];
+          if (r < rows) A[(size_t)r * K + pt.cb[j]] += pt.vals[(size_t)j * P + q];
+        }
+    }
+  }
+  // kept (row block, chunk) pairs and their [hi | lo] swizzled images
+  std::vector<int32_t> rb_ptr(rbs + 1, 0), rb_chunk;
+  std::vector<uint8_t> tiles;
+  for (int64_t b = 0; b < rbs; ++b) {
+    for (int kc = 0; kc < kcs; ++kc) {
+      bool any = false;
+      for (int r = 0; r < kBM && !any; ++r)
+        for (int k = 0; k < kBK; ++k) {
+          const int64_t gk = (int64_t)kc * kBK + k;
+          if (gk < K && A[(size_t)(b * kBM + r) * K + gk] != 0.f) { any = true; break; }
+        }
+      if (!any) continue;
+      rb_chunk.push_back(kc);
+      const size_t off = tiles.size();
+      tiles.resize(off + 2 * kTileBytes, 0);
+      for (int r = 0; r < kBM; ++r)
+        for (int k = 0; k < kBK; ++k) {
+          const int64_t gk = (int64_t)kc * kBK + k;
+          const float x = gk < K ? A[(size_t)(b * kBM + r) * K + gk] : 0.f;
+          const float h = tf32_round(x), l = tf32_round(x - h);
+          memcpy(&tiles[off + swz_offset(r, k)], &h, 4);
+          memcpy(&tiles[off + kTileBytes + swz_offset(r, k)], &l, 4);
+        }
+    }
+    rb_ptr[b + 1] = (int32_t)rb_chunk.size();
+  }
+  const int nts = (int)(p.n / kBN);
+  const size_t b_bytes = (size_t)nts * kcs * 2 * kTileBytes;
+  std::vector<int4> tasks;
+  for (int64_t b = 0; b < rbs; ++b)
+    for (int t = 0; t < nts; ++t) tasks.push_back(make_int4(0, (int)b, t, rb_ptr[b + 1] - rb_ptr[b]));
+  std::stable_sort(tasks.begin(), tasks.end(), [](const int4 &x, const int4 &y) { return x.w > y.w; });
+  p.dense_split = dense_split_for(tasks);
+  auto al = [](size_t x) { return (x + 1023) & ~(size_t)1023; };
+  const size_t o_ptr = al(std::max<size_t>(tiles.size(), 1024));
+  const size_t o_chunk = o_ptr + al((rbs + 1) * 4);
+  const size_t o_b = o_chunk + al(std::max<size_t>(rb_chunk.size(), 1) * 4);
+  const size_t o_tasks = o_b + al(std::max<size_t>(b_bytes, 1024));
+  const size_t o_status = o_tasks + al(std::max<size_t>(tasks.size(), 1) * sizeof(int4));
+  uint8_t *base = nullptr;
+  cuda_check(cudaMalloc(&base, o_status + 1024), "cudaMalloc(dense tiles)");
+  p.a_tiles = base;
+  p.rb_ptr = reinterpret_cast<int32_t *>(base + o_ptr);
+  p.rb_chunk = reinterpret_cast<int32_t *>(base + o_chunk);
+  p.b_tiles = base + o_b;
+  p.status = reinterpret_cast<int *>(base + o_status);
+  p.dense_tasks = reinterpret_cast<int4 *>(base + o_tasks);
+  p.dense_ntasks = (int64_t)tasks.size();
+  if (!tasks.empty())
+    cuda_check(cudaMemcpy(p.dense_tasks, tasks.data(), tasks.size() * sizeof(int4), cudaMemcpyHostToDevice),
+               "upload tasks");
+  if (!tiles.empty()) cuda_check(cudaMemcpy(base, tiles.data(), tiles.size(), cudaMemcpyHostToDevice), "upload tiles");
+  cuda_check(cudaMemcpy(p.rb_ptr, rb_ptr.data(), rb_ptr.size() * 4, cudaMemcpyHostToDevice), "upload tiles");
+  if (!rb_chunk.empty())
+    cuda_check(cudaMemcpy(p.rb_chunk, rb_chunk.data(), rb_chunk.size() * 4, cudaMemcpyHostToDevice), "upload tiles");
+  cuda_check(cudaMemset(p.status, 0, 4), "clear status");
+  p.row_blocks = rbs;
+  p.kept_chunks = (int64_t)rb_chunk.size();
+  p.dev_bytes += o_status + 1024;
+  p.kernel = 3;
 }
 
 sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int64_t pe) {
@@ -277,6 +422,7 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
     cuda_check(cudaMemcpy(base + b_recs + b_items + b_ptr, order.data(), order.size() * 4,
                           cudaMemcpyHostToDevice),
                "upload panel order");
+  if (plan->kernel == 2 && plan->rows > 0 && use_dense(*plan, cf)) build_dense(*plan, cf, pb, rowbits);
   return plan.release();
 }
 
@@ -307,6 +453,14 @@ void launch(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int 
   DeviceGuard dg(p->device);
   const int threads = 32 * p->warps;
   const int nb = (int)p->n;
+  if (p->kernel == 3 && ldc % 4 == 0 && aligned(C, 16)) {
+    const sc::dense::DenseMat m = dense_mat(p, B, ldb, C, ldc);
+    int e = sc_dense_split_b(m, nullptr, 1, m.n_tiles * m.k_chunks, stream);
+    cuda_check((cudaError_t)e, "B tile split launch");
+    e = sc_dense_gemm(m, nullptr, p->dense_tasks, p->dense_ntasks, p->dense_split, accumulate, p->status, stream);
+    cuda_check((cudaError_t)e, "dense tile kernel launch");
+    return;
+  }
   if (p->kernel == 1 && ldb % nb == 0 && aligned(B, 4 * nb)) {
     NarrowFn fn = narrow_kernel((int)p->km, nb);
     fn<<<dim3((unsigned)p->panels), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, p->order, B, ldb,
@@ -444,16 +598,25 @@ void sc_plan_free(sc_plan *p) { delete p; }
 }  // extern "C"
 
 // A set of plans (same device, kernel_m and B width) run as one launch: one
-// CTA per (matrix, panel), heaviest panels first across all matrices.
+// A batch splits its plans into two groups, each run by one launch:
+//  * wide-B plans: one CTA per (matrix, panel), heaviest panels first;
+//  * dense-tile plans: one B-split launch and one tensor-core launch over all
+//    (matrix, row block, n tile) tasks, heaviest first.
 struct sc_batch {
   int device = 0;
   int km = 0, vec = 1, warps = 1, slices = 1;
   int64_t n = 0;
   std::vector<sc_plan *> plans;
-  int64_t tasks = 0;
-  void *dev = nullptr;           // descs | order
+  std::vector<int> wide_ids, dense_ids;  // plan indices per group
+  int64_t tasks = 0;                     // wide group: (matrix, panel) tasks
+  int64_t dense_ntasks = 0;
+  int dense_split = 1, dense_max_tiles = 0;
+  void *dev = nullptr;  // wide descs | wide order | dense mats | dense tasks | status
   sc::WideArgs *descs = nullptr;
   int2 *order = nullptr;
+  sc::dense::DenseMat *dmats = nullptr;
+  int4 *dtasks = nullptr;
+  int *status = nullptr;
   bool bound = false;
   ~sc_batch() {
     if (dev) {
@@ -475,25 +638,35 @@ int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out) {
   const sc_plan *p0 = plans[0];
   require(p0 != nullptr, SC_ERR_ARG, "null plan");
   b->device = p0->device;
-  b->km = (int)p0->km;
   b->n = p0->n;
-  require(p0->kernel == 2, SC_ERR_UNSUPPORTED, "batches run the wide-B kernel (n_cols_b not in {1, 2, 4})");
-  b->vec = p0->vec;
-  b->slices = (int)((b->n + 32 * b->vec - 1) / (32 * b->vec));
-  std::vector<std::pair<int64_t, int2>> tasks;
   for (int32_t i = 0; i < count; ++i) {
     const sc_plan *p = plans[i];
     require(p != nullptr, SC_ERR_ARG, "null plan");
-    require(p->device == b->device && p->km == b->km && p->n == b->n, SC_ERR_UNSUPPORTED,
-            "plans of a batch must share device, kernel_m and n_cols_b");
+    require(p->kernel == 2 || p->kernel == 3, SC_ERR_UNSUPPORTED,
+            "batches run wide-B plans (n_cols_b not in {1, 2, 4})");
+    require(p->device == b->device && p->n == b->n, SC_ERR_UNSUPPORTED,
+            "plans of a batch must share device and n_cols_b");
     b->plans.push_back(plans[i]);
-    for (int64_t lp = 0; lp < p->panels; ++lp) tasks.push_back({p->work[lp], make_int2(i, (int)lp)});
+    (p->kernel == 3 ? b->dense_ids : b->wide_ids).push_back(i);
   }
-  std::stable_sort(tasks.begin(), tasks.end(),
-                   [](const std::pair<int64_t, int2> &x, const std::pair<int64_t, int2> &y) { return x.first > y.first; });
-  b->tasks = (int64_t)tasks.size();
+  // wide group (one kernel_m, one vector width)
+  std::vector<std::pair<int64_t, int2>> tasks;
   int64_t items = 0;
-  for (auto *p : b->plans) items += p->items;
+  if (!b->wide_ids.empty()) {
+    const sc_plan *w0 = plans[b->wide_ids[0]];
+    b->km = (int)w0->km;
+    b->vec = w0->vec;
+    b->slices = (int)((b->n + 32 * b->vec - 1) / (32 * b->vec));
+    for (size_t gi = 0; gi < b->wide_ids.size(); ++gi) {
+      const sc_plan *p = plans[b->wide_ids[gi]];
+      require(p->km == b->km, SC_ERR_UNSUPPORTED, "wide-B plans of a batch must share kernel_m");
+      items += p->items;
+      for (int64_t lp = 0; lp < p->panels; ++lp) tasks.push_back({p->work[lp], make_int2((int)gi, (int)lp)});
+    }
+    std::stable_sort(tasks.begin(), tasks.end(), [](const std::pair<int64_t, int2> &x,
+                                                    const std::pair<int64_t, int2> &y) { return x.first > y.first; });
+  }
+  b->tasks = (int64_t)tasks.size();
   {
     int64_t units = std::max<int64_t>(1, b->tasks * b->slices);
     int w = pow2_at_least((target_warps() + units - 1) / units);
@@ -501,17 +674,45 @@ int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out) {
     w = std::min(w, pow2_at_least(std::max<int64_t>(1, avg_items)));
     b->warps = std::max(1, std::min(w, 8));
   }
+  // dense group
+  std::vector<int4> dtasks;
+  for (size_t gi = 0; gi < b->dense_ids.size(); ++gi) {
+    const sc_plan *p = plans[b->dense_ids[gi]];
+    const int nts = (int)(p->n / sc::dense::kBN);
+    const int kcs = (int)((p->cols + sc::dense::kBK - 1) / sc::dense::kBK);
+    b->dense_max_tiles = std::max(b->dense_max_tiles, nts * kcs);
+    std::vector<int32_t> rbp(p->row_blocks + 1);
+    DeviceGuard dgp(p->device);
+    cuda_check(cudaMemcpy(rbp.data(), p->rb_ptr, rbp.size() * 4, cudaMemcpyDeviceToHost), "read row blocks");
+    for (int64_t r = 0; r < p->row_blocks; ++r)
+      for (int t = 0; t < nts; ++t) dtasks.push_back(make_int4((int)gi, (int)r, t, rbp[r + 1] - rbp[r]));
+  }
+  std::stable_sort(dtasks.begin(), dtasks.end(), [](const int4 &x, const int4 &y) { return x.w > y.w; });
+  b->dense_ntasks = (int64_t)dtasks.size();
+  b->dense_split = dense_split_for(dtasks);
+
   DeviceGuard dg(b->device);
-  const size_t bd = ((count * sizeof(sc::WideArgs)) + 255) & ~(size_t)255;
-  const size_t bo = std::max<size_t>(1, tasks.size()) * sizeof(int2);
-  cuda_check(cudaMalloc(&b->dev, bd + bo), "cudaMalloc(batch)");
-  b->descs = reinterpret_cast<sc::WideArgs *>(b->dev);
-  b->order = reinterpret_cast<int2 *>(static_cast<char *>(b->dev) + bd);
+  auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  const size_t bd = align(std::max<size_t>(1, b->wide_ids.size()) * sizeof(sc::WideArgs));
+  const size_t bo = align(std::max<size_t>(1, tasks.size()) * sizeof(int2));
+  const size_t bm = align(std::max<size_t>(1, b->dense_ids.size()) * sizeof(sc::dense::DenseMat));
+  const size_t bt = align(std::max<size_t>(1, dtasks.size()) * sizeof(int4));
+  cuda_check(cudaMalloc(&b->dev, bd + bo + bm + bt + 256), "cudaMalloc(batch)");
+  char *base = static_cast<char *>(b->dev);
+  b->descs = reinterpret_cast<sc::WideArgs *>(base);
+  b->order = reinterpret_cast<int2 *>(base + bd);
+  b->dmats = reinterpret_cast<sc::dense::DenseMat *>(base + bd + bo);
+  b->dtasks = reinterpret_cast<int4 *>(base + bd + bo + bm);
+  b->status = reinterpret_cast<int *>(base + bd + bo + bm + bt);
+  cuda_check(cudaMemset(b->status, 0, 4), "clear status");
   std::vector<int2> ord(tasks.size());
   for (size_t i = 0; i < tasks.size(); ++i) ord[i] = tasks[i].second;
   if (!ord.empty())
     cuda_check(cudaMemcpy(b->order, ord.data(), ord.size() * sizeof(int2), cudaMemcpyHostToDevice),
                "upload batch order");
+  if (!dtasks.empty())
+    cuda_check(cudaMemcpy(b->dtasks, dtasks.data(), dtasks.size() * sizeof(int4), cudaMemcpyHostToDevice),
+               "upload dense tasks");
   *out = b.release();
   SC_API_END
 }
@@ -521,19 +722,29 @@ int sc_batch_bind(sc_batch *b, const float *const *dB, const int64_t *ldb, float
   SC_API_BEGIN
   require(b != nullptr && dB != nullptr && dC != nullptr && ldb != nullptr && ldc != nullptr, SC_ERR_ARG,
           "null argument");
-  std::vector<sc::WideArgs> d(b->plans.size());
+  std::vector<sc::WideArgs> d;
+  std::vector<sc::dense::DenseMat> dm;
   for (size_t i = 0; i < b->plans.size(); ++i) {
     const sc_plan *p = b->plans[i];
     require(ldb[i] >= p->n && ldc[i] >= p->n, SC_ERR_ARG, "leading dimension smaller than n_cols_b");
     require(p->rows == 0 || (dB[i] != nullptr && dC[i] != nullptr), SC_ERR_ARG, "null B or C");
-    require(ldb[i] % b->vec == 0 && ldc[i] % b->vec == 0 && aligned(dB[i], 4 * b->vec) &&
-                aligned(dC[i], 4 * b->vec),
-            SC_ERR_ARG, "batch operands must be aligned to the vector width (16 bytes for n_cols_b >= 128)");
-    d[i] = wide_args(p, dB[i], ldb[i], dC[i], ldc[i]);
+    if (p->kernel == 3) {
+      require(ldc[i] % 4 == 0 && aligned(dC[i], 16), SC_ERR_ARG, "dense-tile plans need 16-byte aligned C rows");
+      dm.push_back(dense_mat(p, dB[i], ldb[i], dC[i], ldc[i]));
+    } else {
+      require(ldb[i] % b->vec == 0 && ldc[i] % b->vec == 0 && aligned(dB[i], 4 * b->vec) &&
+                  aligned(dC[i], 4 * b->vec),
+              SC_ERR_ARG, "batch operands must be aligned to the vector width (16 bytes for n_cols_b >= 128)");
+      d.push_back(wide_args(p, dB[i], ldb[i], dC[i], ldc[i]));
+    }
   }
   DeviceGuard dg(b->device);
-  cuda_check(cudaMemcpy(b->descs, d.data(), d.size() * sizeof(sc::WideArgs), cudaMemcpyHostToDevice),
-             "upload batch operands");
+  if (!d.empty())
+    cuda_check(cudaMemcpy(b->descs, d.data(), d.size() * sizeof(sc::WideArgs), cudaMemcpyHostToDevice),
+               "upload batch operands");
+  if (!dm.empty())
+    cuda_check(cudaMemcpy(b->dmats, dm.data(), dm.size() * sizeof(sc::dense::DenseMat), cudaMemcpyHostToDevice),
+               "upload batch operands");
   b->bound = true;
   SC_API_END
 }
@@ -542,14 +753,22 @@ int sc_batch_spmm(sc_batch *b, int32_t accumulate, void *stream) {
   SC_API_BEGIN
   require(b != nullptr, SC_ERR_ARG, "null batch");
   require(b->bound, SC_ERR_ARG, "sc_batch_bind must be called before sc_batch_spmm");
-  if (b->tasks == 0) return SC_OK;
   DeviceGuard dg(b->device);
-  WideFn fn = wide_kernel(b->km, b->vec, true);
-  sc::WideArgs none{};
-  fn<<<dim3((unsigned)b->tasks, b->slices), 32 * b->warps, sc::wide_smem_bytes(b->warps, b->km, b->vec),
-       static_cast<cudaStream_t>(stream)>>>(none, b->descs, reinterpret_cast<const int32_t *>(b->order),
-                                            accumulate);
-  cuda_check(cudaGetLastError(), "kernel launch");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (b->dense_ntasks > 0) {
+    sc::dense::DenseMat none{};
+    int e = sc_dense_split_b(none, b->dmats, (int)b->dense_ids.size(), b->dense_max_tiles, s);
+    cuda_check((cudaError_t)e, "B tile split launch");
+    e = sc_dense_gemm(none, b->dmats, b->dtasks, b->dense_ntasks, b->dense_split, accumulate, b->status, s);
+    cuda_check((cudaError_t)e, "dense tile kernel launch");
+  }
+  if (b->tasks > 0) {
+    WideFn fn = wide_kernel(b->km, b->vec, true);
+    sc::WideArgs none{};
+    fn<<<dim3((unsigned)b->tasks, b->slices), 32 * b->warps, sc::wide_smem_bytes(b->warps, b->km, b->vec), s>>>(
+        none, b->descs, reinterpret_cast<const int32_t *>(b->order), accumulate);
+    cuda_check(cudaGetLastError(), "kernel launch");
+  }
   SC_API_END
 }
 

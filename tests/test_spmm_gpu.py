@@ -76,7 +76,7 @@ def test_config3_large_b(cuda, shape, N):
     for m in range(1, 7):
         cf = sc.csr_to_compressed_format_converter(h, m, 1)
         C, plan = run(cf, B, cuda)
-        assert plan.info["kernel"] == 2
+        assert plan.info["kernel"] in (2, 3)  # 3: dense-tile tensor-core path (N = 128)
         assert_parity(C, a, B)
 
 
@@ -236,7 +236,8 @@ def test_batch_layer_stack_one_launch(cuda):
         assert_parity(C.cpu().numpy() / 2, a, B)
 
 
-def test_batch_rejects_mixed_plans(cuda):
+def test_batch_rejects_mixed_plans(cuda, monkeypatch):
+    monkeypatch.setenv("SC_DENSE", "0")
     a, _ = wl.config1()
     h = to_csr_handle(a)
     p1 = sc.SpMMPlan(sc.csr_to_compressed_format_converter(h, 4, 1), 128)
@@ -274,3 +275,37 @@ def test_autotune_kernel_m(cuda):
     a, B = wl.config3((2048, 512), 128)
     best, times = tuning.autotune_kernel_m(to_csr_handle(a), 128, candidates=(1, 4), reps=3)
     assert best in (1, 4) and set(times) == {1, 4} and all(t > 0 for t in times.values())
+
+
+@pytest.mark.parametrize("dense", ["0", "1"])
+def test_config4_per_plan_paths(cuda, monkeypatch, dense):
+    """A few stack matrices through each path explicitly (wide FFMA / dense tiles)."""
+    import torch
+    monkeypatch.setenv("SC_DENSE", dense)
+    for name, a, B in wl.config4(128)[:6]:
+        cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+        plan = sc.SpMMPlan(cf, 128)
+        assert plan.info["kernel"] == (3 if dense == "1" else 2)
+        C = plan.spmm(torch.from_numpy(B).to(cuda))
+        torch.cuda.synchronize()
+        assert_parity(C.cpu().numpy(), a, B)
+
+
+def test_batch_mixed_dense_and_wide(cuda, monkeypatch):
+    """One batch holding dense-tile and wide-B plans (two groups, one launch each)."""
+    import torch
+    mats = wl.config4(128)[:8]
+    plans, Bs, Cs = [], [], []
+    for i, (name, a, B) in enumerate(mats):
+        monkeypatch.setenv("SC_DENSE", "1" if i % 2 else "0")
+        cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+        plans.append(sc.SpMMPlan(cf, 128))
+        Bs.append(torch.from_numpy(B).to(cuda))
+        Cs.append(torch.full((a[0], 128), float("nan"), device=cuda))
+    assert {p.info["kernel"] for p in plans} == {2, 3}
+    batch = sc.SpMMBatch(plans)
+    batch.bind(Bs, Cs)
+    batch.spmm()
+    torch.cuda.synchronize()
+    for (name, a, B), C in zip(mats, Cs):
+        assert_parity(C.cpu().numpy(), a, B)
