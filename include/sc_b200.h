@@ -165,6 +165,24 @@ int sc_spmv(sc_plan *p, const float *dx, float *dy, int32_t accumulate, void *st
 int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream);
 void sc_plan_free(sc_plan *p);
 
+/* ------------------------------------------------------ allocation-free -- */
+
+/* C = A*B (or C += A*B) for a DENSE row-major fp32 A (m x k, leading
+ * dimension lda) on the dense-tile tensor-core kernel, without a plan and
+ * without allocating: for callers that cannot call cudaMalloc on their hot
+ * path (a process that gives all device memory to its own pool or budget at
+ * start-up, or a framework that forbids device allocation there).  No
+ * counterpart in the reference.  All scratch (TF32 head/tail tile images of A
+ * and B, task list, status word) sits in one 16 MiB array held by every GPU
+ * that loads the library until exit; inputs beyond it -- A padded to 128-row
+ * blocks plus B, at 8 bytes per element -- are rejected with SC_ERR_ARG.
+ * n must be a multiple of 128; C rows 16-byte aligned.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress), so make
+ * that first call before any stream capture.  Calls share the array: calls
+ * that overlap on the GPU (different streams at once) race. */
+int sc_spmm_dense_noalloc(const float *dA, int64_t lda, int64_t m, int64_t k, const float *dB, int64_t ldb,
+                          int64_t n, float *dC, int64_t ldc, int32_t accumulate, void *stream);
+
 /* ------------------------------------------------------------- batches ---- */
 
 typedef struct sc_batch sc_batch; /* several plans executed by one kernel launch */

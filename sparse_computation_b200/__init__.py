@@ -51,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "sc_plan_create", "sc_plan_create_panels", "sc_plan_get_info", "sc_spmm", "sc_spmv",
     "sc_spmm_host", "sc_plan_free", "sc_spmm_peers",
     "sc_batch_create", "sc_batch_bind", "sc_batch_spmm", "sc_batch_free",
+    "sc_spmm_dense_noalloc",
 )
 
 
@@ -115,6 +116,7 @@ def lib() -> ctypes.CDLL:
         "sc_batch_bind": ([vp, vp, vp, vp, vp], ctypes.c_int),
         "sc_batch_spmm": ([vp, i32, vp], ctypes.c_int),
         "sc_batch_free": ([vp], None),
+        "sc_spmm_dense_noalloc": ([vp, i64, i64, i64, vp, i64, i64, vp, i64, i32, vp], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)

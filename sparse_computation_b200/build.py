@@ -27,7 +27,8 @@ CXXFLAGS = ["-O3", "-std=c++17", "-fPIC", "-pthread", "-Wall", "-Wno-unused-func
 
 HOST_SOURCES = ["sc_host.cpp"]
 # (source, extra flags, object name): sc_inst.cu is compiled once per kernel_m.
-CUDA_SOURCES = [("sc_plan.cu", [], "sc_plan.cu.o"), ("sc_dense.cu", [], "sc_dense.cu.o")] + [
+CUDA_SOURCES = [("sc_plan.cu", [], "sc_plan.cu.o"), ("sc_dense.cu", [], "sc_dense.cu.o"),
+                ("sc_noalloc.cu", [], "sc_noalloc.cu.o")] + [
     ("sc_inst.cu", [f"-DSC_KM={km}"], f"sc_inst_km{km}.cu.o") for km in range(1, 7)]
 
 
