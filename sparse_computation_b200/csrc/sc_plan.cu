@@ -57,6 +57,13 @@ struct sc_plan {
   const int32_t *item_ptr = nullptr;
   const int32_t *order = nullptr;
   float *stage_b = nullptr, *stage_c = nullptr;
+  // Row-chunked panel orders for the host entry point, so that the copy of a
+  // finished chunk of C overlaps the kernels of the next chunks.
+  static constexpr int kHostChunks = 4;
+  int32_t *chunk_order = nullptr;
+  std::vector<int64_t> chunk_off;  // kHostChunks + 1 offsets into chunk_order (= panel ranges)
+  cudaStream_t side = nullptr;
+  cudaEvent_t chunk_ev[kHostChunks] = {};
   std::vector<int64_t> work;  // per local panel, for batch scheduling
   // Dense-tile tensor-core path (kernel == 3): swizzled A_hi/A_lo tiles of
   // the kept (row block, K-chunk) pairs, per-call B tile images, error word.
@@ -69,12 +76,16 @@ struct sc_plan {
   int64_t dense_ntasks = 0;
   int dense_split = 1;          // CTAs (cluster) per task
   ~sc_plan() {
-    if (dev || stage_b || stage_c || a_tiles) {
+    if (dev || stage_b || stage_c || a_tiles || chunk_order || side) {
       int prev;
       bool ok = cudaGetDevice(&prev) == cudaSuccess;
       if (ok && prev != device) cudaSetDevice(device);
       if (dev) cudaFree(dev);
       if (a_tiles) cudaFree(a_tiles);  // one allocation: tiles | rb_ptr | rb_chunk | b_tiles | status
+      if (chunk_order) cudaFree(chunk_order);
+      for (auto &e : chunk_ev)
+        if (e) cudaEventDestroy(e);
+      if (side) cudaStreamDestroy(side);
       if (stage_b) cudaFree(stage_b);
       if (stage_c) cudaFree(stage_c);
       if (ok && prev != device) cudaSetDevice(prev);
@@ -424,6 +435,21 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
                           cudaMemcpyHostToDevice),
                "upload panel order");
   if (plan->kernel == 2 && plan->rows > 0 && use_dense(*plan, cf)) build_dense(*plan, cf, pb, rowbits);
+  if (plan->kernel != 3 && plan->panels >= sc_plan::kHostChunks) {
+    // panels split into kHostChunks contiguous row ranges, heaviest first inside each
+    std::vector<int32_t> co;
+    plan->chunk_off.push_back(0);
+    for (int c = 0; c < sc_plan::kHostChunks; ++c) {
+      const int64_t a0 = plan->panels * c / sc_plan::kHostChunks, a1 = plan->panels * (c + 1) / sc_plan::kHostChunks;
+      std::vector<int32_t> part;
+      for (int64_t q = a0; q < a1; ++q) part.push_back((int32_t)q);
+      std::stable_sort(part.begin(), part.end(), [&](int32_t x, int32_t y) { return work[x] > work[y]; });
+      co.insert(co.end(), part.begin(), part.end());
+      plan->chunk_off.push_back((int64_t)co.size());
+    }
+    cuda_check(cudaMalloc(&plan->chunk_order, co.size() * 4), "cudaMalloc(chunk order)");
+    cuda_check(cudaMemcpy(plan->chunk_order, co.data(), co.size() * 4, cudaMemcpyHostToDevice), "upload chunks");
+  }
   return plan.release();
 }
 
@@ -446,9 +472,19 @@ sc::WideArgs wide_args(const sc_plan *p, const float *B, int64_t ldb, float *C, 
   return a;
 }
 
+void launch_panels(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int accumulate,
+                   cudaStream_t stream, const int32_t *order, int64_t count);
+
 void launch(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int accumulate,
             cudaStream_t stream) {
+  launch_panels(p, B, ldb, C, ldc, accumulate, stream, p->order, p->panels);
+}
+
+// Runs the panels listed in order[0..count) (all panels: p->order).
+void launch_panels(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int accumulate,
+                   cudaStream_t stream, const int32_t *order, int64_t count) {
   require(ldb >= p->n && ldc >= p->n, SC_ERR_ARG, "leading dimension smaller than n_cols_b");
+  if (count == 0) return;
   if (p->panels == 0 || p->rows == 0) return;  // nothing to write (C may be an empty buffer)
   require(B != nullptr && C != nullptr, SC_ERR_ARG, "null B or C");
   DeviceGuard dg(p->device);
@@ -464,8 +500,8 @@ void launch(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int 
   }
   if (p->kernel == 1 && ldb % nb == 0 && aligned(B, 4 * nb)) {
     NarrowFn fn = narrow_kernel((int)p->km, nb);
-    fn<<<dim3((unsigned)p->panels), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, p->order, B, ldb,
-                                                           C, ldc, p->rows, accumulate);
+    fn<<<dim3((unsigned)count), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, order, B, ldb, C, ldc,
+                                                       p->rows, accumulate);
   } else {
     int vec = p->kernel == 2 ? p->vec : 1;
     while (vec > 1 && !(p->n % vec == 0 && ldb % vec == 0 && ldc % vec == 0 && aligned(B, 4 * vec) &&
@@ -474,8 +510,8 @@ void launch(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int 
     const int slices = (int)((p->n + 32 * vec - 1) / (32 * vec));
     WideFn fn = wide_kernel((int)p->km, vec, false);
     const size_t smem = sc::wide_smem_bytes(p->warps, (int)p->km, vec);
-    fn<<<dim3((unsigned)p->panels, slices), threads, smem, stream>>>(wide_args(p, B, ldb, C, ldc), nullptr,
-                                                                     p->order, accumulate);
+    fn<<<dim3((unsigned)count, slices), threads, smem, stream>>>(wide_args(p, B, ldb, C, ldc), nullptr, order,
+                                                                 accumulate);
   }
   cuda_check(cudaGetLastError(), "kernel launch");
 }
@@ -588,9 +624,31 @@ int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream) {
   if (!p->stage_b) cuda_check(cudaMalloc(&p->stage_b, std::max<size_t>(bb, 16)), "cudaMalloc(B staging)");
   if (!p->stage_c) cuda_check(cudaMalloc(&p->stage_c, std::max<size_t>(cb, 16)), "cudaMalloc(C staging)");
   if (bb) cuda_check(cudaMemcpyAsync(p->stage_b, hB, bb, cudaMemcpyHostToDevice, s), "copy B to device");
-  launch(p, p->stage_b, p->n, p->stage_c, p->n, 0, s);
-  if (cb) cuda_check(cudaMemcpyAsync(hC, p->stage_c, cb, cudaMemcpyDeviceToHost, s), "copy C to host");
-  cuda_check(cudaStreamSynchronize(s), "stream synchronize");
+  if (!p->chunk_order || cb == 0) {
+    launch(p, p->stage_b, p->n, p->stage_c, p->n, 0, s);
+    if (cb) cuda_check(cudaMemcpyAsync(hC, p->stage_c, cb, cudaMemcpyDeviceToHost, s), "copy C to host");
+    cuda_check(cudaStreamSynchronize(s), "stream synchronize");
+  } else {
+    // row chunks: kernel of chunk c on `s`, then its C rows to the host on a
+    // side stream while the next chunks compute
+    if (!p->side) {
+      cuda_check(cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking), "create side stream");
+      for (auto &e : p->chunk_ev) cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "create event");
+    }
+    for (int c = 0; c < sc_plan::kHostChunks; ++c) {
+      const int64_t a0 = p->chunk_off[c], a1 = p->chunk_off[c + 1];
+      launch_panels(p, p->stage_b, p->n, p->stage_c, p->n, 0, s, p->chunk_order + a0, a1 - a0);
+      cuda_check(cudaEventRecord(p->chunk_ev[c], s), "record event");
+      cuda_check(cudaStreamWaitEvent(p->side, p->chunk_ev[c], 0), "wait event");
+      const int64_t r0 = std::min<int64_t>(p->rows, a0 * p->km), r1 = std::min<int64_t>(p->rows, a1 * p->km);
+      if (r1 > r0)
+        cuda_check(cudaMemcpyAsync(hC + r0 * p->n, p->stage_c + r0 * p->n, (size_t)(r1 - r0) * p->n * sizeof(float),
+                                   cudaMemcpyDeviceToHost, p->side),
+                   "copy C to host");
+    }
+    cuda_check(cudaStreamSynchronize(p->side), "stream synchronize");
+    cuda_check(cudaStreamSynchronize(s), "stream synchronize");
+  }
   SC_API_END
 }
 
