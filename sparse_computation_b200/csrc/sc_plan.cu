@@ -297,6 +297,29 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
   p.kernel = 3;
 }
 
+// Warps per CTA (<= max_w, powers of two) minimising waves(W) * (2 + items/W)
+// for `units` CTAs averaging `avg_items` work items each; the device must be
+// current.
+int wave_model_warps(int km, int vec, bool batch, int64_t units, double avg_items, int max_w) {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  WideFn fn = wide_kernel(km, vec, batch);
+  double best = 0;
+  int best_w = 1;
+  for (int w = 1; w <= max_w; w <<= 1) {
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 32 * w, sc::wide_smem_bytes(w, km, vec));
+    const int64_t resident = std::max<int64_t>(1, (int64_t)per_sm * sms);
+    const double t = (double)((units + resident - 1) / resident) * (2.0 + avg_items / w);
+    if (w == 1 || t < best) {
+      best = t;
+      best_w = w;
+    }
+  }
+  return best_w;
+}
+
 sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int64_t pe) {
   const int km = cf.kernel_m;
   require(km >= 1 && km <= 6, SC_ERR_UNSUPPORTED, "plans support kernel_m 1..6");
@@ -412,6 +435,14 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
 
   // One device allocation: recs | items | item_ptr | order.
   DeviceGuard dg(device);
+  // Warps per CTA from a wave model: time ~ waves(W) * (2 + items/W), where a
+  // wave is the CTAs resident at once (occupancy at W warps) and "2" is the
+  // per-CTA start-up chain (panel -> item range -> records -> B rows) in item
+  // units.  Avoids e.g. a thin second wave for one rank's share of a
+  // row-partitioned matrix.
+  if (plan->kernel == 2 && plan->panels > 0)
+    plan->warps = wave_model_warps(km, plan->vec, false, plan->panels * slices,
+                                   (double)plan->items / (double)plan->panels, plan->warps);
   auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
   const size_t b_recs = align(recs.size() * 4);
   const size_t b_items = align(std::max<size_t>(1, items.size()) * sizeof(int2));
@@ -731,6 +762,8 @@ int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out) {
     int w = pow2_at_least((target_warps() + units - 1) / units);
     int64_t avg_items = b->tasks ? (items + b->tasks - 1) / b->tasks : 1;
     w = std::min(w, pow2_at_least(std::max<int64_t>(1, avg_items)));
+    // (the single-plan wave model below mispredicted the mixed-size batches of
+    // config 3: 25 -> 37 us; batches keep the warp-count rule)
     b->warps = std::max(1, std::min(w, 8));
   }
   // dense group
