@@ -53,9 +53,10 @@ def parse():
     p.add_argument("--sweep-small", action="store_true",
                    help="config 2 table: every sparsity x N in {1,2,4}, single warm launch, CUDA-graph "
                         "replay, and cuSPARSE (one JSON line with a 'sweep' list)")
-    p.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+    p.add_argument("--exchange", choices=["peer", "peer-barrier", "nccl"], default="peer",
                    help="N>1 row partition: C blocks stored to peers by the SpMM kernel itself over NVLink "
-                        "(symmetric memory) or gathered afterwards with NCCL all-gather")
+                        "(symmetric memory) and completion flags (peer) or a barrier (peer-barrier), or "
+                        "gathered afterwards with NCCL all-gather (nccl)")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU work of the bounded cpu_baseline sample")
     return p.parse_args()
@@ -88,9 +89,9 @@ def workload(cfg: int, n_cols_b):
 from sparse_computation_b200.partition import balanced_panel_cuts, lpt_assign, row_slice  # noqa: E402
 
 
-def symmetric_buffer(shape, dev):
-    """A float32 buffer allocated in torch symmetric memory (peer-mapped on
-    every rank) and its rendezvous handle."""
+def symmetric_buffer(shape, dev, dtype=None):
+    """A buffer (float32 by default) allocated in torch symmetric memory
+    (peer-mapped on every rank) and its rendezvous handle."""
     import torch
     import torch.distributed as dist
     import torch.distributed._symmetric_memory as symm_mem
@@ -99,7 +100,7 @@ def symmetric_buffer(shape, dev):
         symm_mem.enable_symm_mem_for_group(group.group_name)
     except Exception:
         pass
-    t = symm_mem.empty(shape, dtype=torch.float32, device=dev)
+    t = symm_mem.empty(shape, dtype=dtype or torch.float32, device=dev)
     hdl = symm_mem.rendezvous(t, group.group_name)
     return t, hdl
 
@@ -455,11 +456,16 @@ def main():
             max_rows = max(min(cuts[r + 1] * mk, m) - min(cuts[r] * mk, m) for r in range(world))
             j = {"km": mk, "plan": plan, "B": torch.from_numpy(B).to(dev), "rows": r1 - r0, "max_rows": max_rows,
                  "m": m, "nnz_local": len(blk[3]), "Bhost": B, "cuts": cuts, "K": a[1]}
-            if world > 1 and args.exchange == "peer":
+            if world > 1 and args.exchange.startswith("peer"):
                 full, hdl = symmetric_buffer((m, N), dev)
                 j["full"], j["hdl"] = full, hdl
                 j["C"] = full[r0:r1]
                 j["peers"] = [int(hdl.buffer_ptrs[q]) + r0 * N * 4 for q in range(world) if q != rank]
+                flags, fh = symmetric_buffer((world,), dev, torch.int32)
+                flags.zero_()
+                j["flags"], j["flag_ptrs"] = flags, [int(fh.buffer_ptrs[q]) + rank * 4 for q in range(world)]
+                j["status"] = torch.zeros(1, dtype=torch.int32, device=dev)
+                fh.barrier(channel=0)
             else:
                 j["gather"] = torch.empty((world, max_rows, N), device=dev)
                 j["C"] = j["gather"][rank, : j["rows"]] if world > 1 else torch.empty((j["rows"], N), device=dev)
@@ -474,7 +480,9 @@ def main():
             batches.append(bt)
     t_setup = time.perf_counter() - t_setup
 
-    peer_mode = world > 1 and not layers and args.exchange == "peer"
+    peer_mode = world > 1 and not layers and args.exchange.startswith("peer")
+    use_flags = args.exchange == "peer"
+    epoch = [0]
 
     def launch_all(stream):
         if batches:
@@ -483,14 +491,22 @@ def main():
         else:
             for j in jobs:
                 if peer_mode:  # the kernel stores each C tile locally and into every peer's C
-                    j["plan"].spmm_peers(j["B"], j["C"], j["peers"], stream=stream)
+                    if use_flags:
+                        epoch[0] += 1
+                        j["plan"].spmm_peers(j["B"], j["C"], j["peers"], stream=stream, flag_ptrs=j["flag_ptrs"],
+                                             epoch=epoch[0])
+                    else:
+                        j["plan"].spmm_peers(j["B"], j["C"], j["peers"], stream=stream)
                 else:
                     j["plan"].spmm(j["B"], j["C"], stream=stream)
 
     def gather_all():
         if peer_mode:
             for j in jobs:
-                j["hdl"].barrier(channel=0)  # all ranks' peer stores have landed
+                if use_flags:  # every rank's last CTA has published its epoch here
+                    sc.wait_flags(j["flags"].data_ptr(), world, epoch[0], j["status"].data_ptr(), stream)
+                else:
+                    j["hdl"].barrier(channel=0)  # all ranks' peer stores have landed
         elif world > 1 and not layers:
             for j in jobs:
                 # in place: this rank's block already sits at its slot
@@ -586,6 +602,9 @@ def main():
             h2d = sum(j["Bhost"].nbytes for j in jobs)
             d2h = sum(j["m"] * N * 4 for j in jobs) if (rank == 0 or layers) else 0
 
+    exchange_status = 0
+    if peer_mode and use_flags:
+        exchange_status = max(int(j["status"].item()) for j in jobs)  # 5: a flag wait expired
     # ---- reduce over ranks (max time)
     t = torch.tensor([step_ms, kern_ms, e2e_s], dtype=torch.float64, device=dev)
     if world > 1:
@@ -623,6 +642,7 @@ def main():
                                   {"kernel_m": "auto (measured per matrix)", "chosen": sorted({j["km"] for j in jobs}),
                                    "kernel_n": kn}),
                    "n_cols_b": N, "nnz": total_nnz,
+                   "exchange": args.exchange if world > 1 and not layers else None,
                    "parallelism": ("1 GPU" if world == 1 else
                                    f"whole matrices sharded over {world} GPUs (LPT by nnz), no collective"
                                    if layers else
@@ -642,7 +662,8 @@ def main():
                      "fp32_frac": local_flops / (kern_ms * 1e-3) / 1e12 / fp32_peak},
         "e2e": {"value": e2e_value, "unit": "GFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_s * 1e3},
-        "gpu_launches": args.steps * (len(batches) if batches else len(jobs)),
+        "gpu_launches": args.steps * (len(batches) if batches else len(jobs)) * (2 if peer_mode and use_flags else 1),
+        "exchange_status": exchange_status,
         "clocks": clk,
         "setup_s": t_setup,
     }

@@ -155,7 +155,18 @@ int sc_spmm(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc,
  * stream before reading C.  Wide-B plans only.  The reference has no
  * multi-GPU path; this replaces "SpMM then NCCL all-gather". */
 int sc_spmm_peers(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc, float *const *peer_C,
-                  int32_t npeers, int32_t accumulate, void *stream);
+                  int32_t npeers, int *const *flag_dst, int32_t nflags, int32_t epoch, int32_t accumulate,
+                  void *stream);
+/* Completion signal of sc_spmm_peers (nflags > 0): right after the product
+ * kernel, a one-warp kernel on the same stream stores `epoch` (release,
+ * system scope) into flag_dst[0..nflags) -- this rank's slot in each GPU's
+ * int flag array (peer-mapped), own GPU included.
+ * sc_wait_flags then waits on the stream (one warp, acquire, bounded; on
+ * expiry it writes 5 to *status) until flags[0..n) of this GPU have all
+ * reached `epoch` (wrap-safe): every rank's C tiles have landed here.  Use a
+ * new epoch per product.  Replaces a separate cross-GPU barrier after the
+ * product.  No counterpart in the reference (no multi-GPU code there). */
+int sc_wait_flags(const int *flags, int32_t n, int32_t epoch, int *status, void *stream);
 /* y = A*x or y += A*x (plan built with n_cols_b == 1). */
 int sc_spmv(sc_plan *p, const float *dx, float *dy, int32_t accumulate, void *stream);
 /* End-to-end product from HOST buffers: copies hB (K x N, dense row-major)

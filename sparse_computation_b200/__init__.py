@@ -49,7 +49,7 @@ EXPORTED_SYMBOLS = (
     "sc_cf_pattern_sizes", "sc_cf_pattern_arrays", "sc_cf_real_nnz", "sc_cf_free",
     "sc_companion_mtx_path", "sc_cf_write_binary", "sc_cf_load_binary",
     "sc_plan_create", "sc_plan_create_panels", "sc_plan_get_info", "sc_spmm", "sc_spmv",
-    "sc_spmm_host", "sc_plan_free", "sc_spmm_peers",
+    "sc_spmm_host", "sc_plan_free", "sc_spmm_peers", "sc_wait_flags",
     "sc_batch_create", "sc_batch_bind", "sc_batch_spmm", "sc_batch_free",
     "sc_spmm_dense_noalloc",
 )
@@ -109,7 +109,8 @@ def lib() -> ctypes.CDLL:
         "sc_plan_get_info": ([vp, P(_PlanInfo)], ctypes.c_int),
         "sc_spmm": ([vp, vp, i64, vp, i64, i32, vp], ctypes.c_int),
         "sc_spmv": ([vp, vp, vp, i32, vp], ctypes.c_int),
-        "sc_spmm_peers": ([vp, vp, i64, vp, i64, vp, i32, i32, vp], ctypes.c_int),
+        "sc_spmm_peers": ([vp, vp, i64, vp, i64, vp, i32, vp, i32, i32, i32, vp], ctypes.c_int),
+        "sc_wait_flags": ([vp, i32, i32, vp, vp], ctypes.c_int),
         "sc_spmm_host": ([vp, vp, vp, vp], ctypes.c_int),
         "sc_plan_free": ([vp], None),
         "sc_batch_create": ([vp, i32, P(vp)], ctypes.c_int),
@@ -323,6 +324,13 @@ def load_cfmtx_matrices(cfmtx_path) -> Tuple[CSR, CompressedFormat]:
 
 # ------------------------------------------------------------------ plan --
 
+def wait_flags(flags_ptr: int, n: int, epoch: int, status_ptr: int, stream) -> None:
+    """Stream-ordered bounded wait until the n ints at device address
+    flags_ptr have all reached `epoch` (sc_wait_flags)."""
+    _check(lib().sc_wait_flags(ctypes.c_void_p(flags_ptr), n, int(epoch), ctypes.c_void_p(status_ptr),
+                               ctypes.c_void_p(stream.cuda_stream)))
+
+
 def _torch():
     import torch
     return torch
@@ -377,18 +385,21 @@ class SpMMPlan:
                              self._stream(stream)))
         return C
 
-    def spmm_peers(self, B, C, peer_ptrs, accumulate: bool = False, stream=None):
+    def spmm_peers(self, B, C, peer_ptrs, accumulate: bool = False, stream=None, flag_ptrs=(), epoch=0):
         """spmm() that also stores C into peer GPUs' buffers (device addresses
-        `peer_ptrs`, each pointing at the same first row as C)."""
+        `peer_ptrs`, each pointing at the same first row as C); with
+        `flag_ptrs`, the last CTA then stores `epoch` into each flag address
+        (see wait_flags)."""
         torch = _torch()
         if B.dtype != torch.float32 or C.dtype != torch.float32 or B.stride(1) != 1 or C.stride(1) != 1:
             raise ScError(SC_ERR_ARG, "B and C must be float32 with unit column stride")
         if tuple(B.shape) != (self.cols, self.n) or tuple(C.shape) != (self.rows, self.n):
             raise ScError(SC_ERR_ARG, "operand shapes do not match the plan")
         arr = (ctypes.c_void_p * max(1, len(peer_ptrs)))(*peer_ptrs)
+        fl = (ctypes.c_void_p * max(1, len(flag_ptrs)))(*flag_ptrs)
         _check(lib().sc_spmm_peers(self._h, ctypes.c_void_p(B.data_ptr()), B.stride(0),
-                                   ctypes.c_void_p(C.data_ptr()), C.stride(0), arr, len(peer_ptrs),
-                                   1 if accumulate else 0, self._stream(stream)))
+                                   ctypes.c_void_p(C.data_ptr()), C.stride(0), arr, len(peer_ptrs), fl,
+                                   len(flag_ptrs), int(epoch), 1 if accumulate else 0, self._stream(stream)))
         return C
 
     def spmv(self, x, y=None, accumulate: bool = False, stream=None):

@@ -609,8 +609,11 @@ int sc_spmm(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc, in
 }
 
 int sc_spmm_peers(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc, float *const *peer_C,
-                  int32_t npeers, int32_t accumulate, void *stream) {
+                  int32_t npeers, int *const *flag_dst, int32_t nflags, int32_t epoch, int32_t accumulate,
+                  void *stream) {
   SC_API_BEGIN
+  require(nflags >= 0 && nflags <= sc::kMaxPeers + 1 && (nflags == 0 || flag_dst != nullptr), SC_ERR_ARG,
+          "nflags must be 0..8 with a flag pointer list");
   require(p != nullptr, SC_ERR_ARG, "null plan");
   require(npeers >= 0 && npeers <= sc::kMaxPeers, SC_ERR_ARG, "npeers must be 0..7");
   require(npeers == 0 || peer_C != nullptr, SC_ERR_ARG, "null peer list");
@@ -629,10 +632,28 @@ int sc_spmm_peers(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t l
   sc::WideArgs a = wide_args(p, dB, ldb, dC, ldc);
   a.npeers = npeers;
   for (int i = 0; i < npeers; ++i) a.peers[i] = peer_C[i];
+  sc::FlagList fl;
+  fl.n = nflags;
+  for (int i = 0; i < nflags; ++i) {
+    require(flag_dst[i] != nullptr && aligned(flag_dst[i], 4), SC_ERR_ARG, "bad flag pointer");
+    fl.dst[i] = flag_dst[i];
+  }
   const int slices = (int)((p->n + 32 * vec - 1) / (32 * vec));
   WideFn fn = wide_kernel((int)p->km, vec, false);
   fn<<<dim3((unsigned)p->panels, slices), 32 * p->warps, sc::wide_smem_bytes(p->warps, (int)p->km, vec),
        static_cast<cudaStream_t>(stream)>>>(a, nullptr, p->order, accumulate);
+  cuda_check(cudaGetLastError(), "kernel launch");
+  if (nflags > 0) {
+    sc::signal_flags_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fl, epoch);
+    cuda_check(cudaGetLastError(), "kernel launch");
+  }
+  SC_API_END
+}
+
+int sc_wait_flags(const int *flags, int32_t n, int32_t epoch, int *status, void *stream) {
+  SC_API_BEGIN
+  require(flags != nullptr && status != nullptr && n >= 1 && n <= 1024, SC_ERR_ARG, "bad flag wait arguments");
+  sc::wait_flags_kernel<<<1, 32 * ((n + 31) / 32), 0, static_cast<cudaStream_t>(stream)>>>(flags, n, epoch, status);
   cuda_check(cudaGetLastError(), "kernel launch");
   SC_API_END
 }

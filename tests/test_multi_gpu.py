@@ -43,7 +43,7 @@ def _worker(rank, world, port, mode, result):
         cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*pt.row_slice(a, r0, r1)), 4, 1)
         plan = sc.SpMMPlan(cf, 128, device=rank)
         Bt = torch.from_numpy(B).to(dev)
-        if mode == "peer":
+        if mode in ("peer", "signal"):
             import torch.distributed._symmetric_memory as symm_mem
             g = dist.group.WORLD
             try:
@@ -53,9 +53,26 @@ def _worker(rank, world, port, mode, result):
             full = symm_mem.empty((m, 128), dtype=torch.float32, device=dev)
             hdl = symm_mem.rendezvous(full, g.group_name)
             peers = [int(hdl.buffer_ptrs[q]) + r0 * 128 * 4 for q in range(world) if q != rank]
-            for _ in range(2):
-                plan.spmm_peers(Bt, full[r0:r1], peers)
-                hdl.barrier(channel=0)
+            if mode == "peer":
+                for _ in range(2):
+                    plan.spmm_peers(Bt, full[r0:r1], peers)
+                    hdl.barrier(channel=0)
+            else:
+                flags = symm_mem.empty((world,), dtype=torch.int32, device=dev)
+                fh = symm_mem.rendezvous(flags, g.group_name)
+                flags.zero_()
+                status = torch.zeros(1, dtype=torch.int32, device=dev)
+                fh.barrier(channel=0)
+                fptrs = [int(fh.buffer_ptrs[q]) + rank * 4 for q in range(world)]
+                stream = torch.cuda.current_stream()
+                for epoch in (1, 2, 3):
+                    full.zero_() if epoch == 3 else None
+                    if epoch == 3:
+                        fh.barrier(channel=0)  # every rank cleared its C before new stores arrive
+                    plan.spmm_peers(Bt, full[r0:r1], peers, flag_ptrs=fptrs, epoch=epoch)
+                    sc.wait_flags(flags.data_ptr(), world, epoch, status.data_ptr(), stream)
+                torch.cuda.synchronize()
+                assert int(status.item()) == 0
             C = full
         else:
             C = pt.gather_row_blocks(plan.spmm(Bt), cuts, rank, world, 4, m)
@@ -68,7 +85,7 @@ def _worker(rank, world, port, mode, result):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["peer", "nccl"])
+@pytest.mark.parametrize("mode", ["peer", "signal", "nccl"])
 def test_row_partition_two_gpus(mode):
     import torch
     if torch.cuda.device_count() < 2:
