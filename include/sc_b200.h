@@ -214,6 +214,22 @@ int sc_batch_bind(sc_batch *b, const float *const *dB, const int64_t *ldb, float
 int sc_batch_spmm(sc_batch *b, int32_t accumulate, void *stream);
 void sc_batch_free(sc_batch *b);
 
+/* ---------------------------------------------------------------- graphs -- */
+
+typedef struct sc_graph sc_graph; /* captured CUDA graph of products with fixed operands */
+
+/* Captures `repeat` back-to-back products (sc_spmm of a plan with these
+ * operands, or sc_batch_spmm of a bound batch) into one CUDA graph, so that
+ * a whole pattern-group schedule -- or many tiny 512-wide layers -- costs one
+ * launch.  Replaces the reference's per-trial launches
+ * (example_cuda/spmm_demo_gpu_utils.h:1700-1712); the reference has no
+ * graphs. */
+int sc_graph_capture_plan(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc, int32_t accumulate,
+                          int32_t repeat, sc_graph **out);
+int sc_graph_capture_batch(sc_batch *b, int32_t accumulate, int32_t repeat, sc_graph **out);
+int sc_graph_launch(sc_graph *g, void *stream);
+void sc_graph_free(sc_graph *g);
+
 #ifdef __cplusplus
 }
 #endif

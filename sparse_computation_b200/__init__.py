@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "sc_spmm_host", "sc_plan_free", "sc_spmm_peers", "sc_wait_flags",
     "sc_batch_create", "sc_batch_bind", "sc_batch_spmm", "sc_batch_free",
     "sc_spmm_dense_noalloc",
+    "sc_graph_capture_plan", "sc_graph_capture_batch", "sc_graph_launch", "sc_graph_free",
 )
 
 
@@ -117,6 +118,10 @@ def lib() -> ctypes.CDLL:
         "sc_batch_bind": ([vp, vp, vp, vp, vp], ctypes.c_int),
         "sc_batch_spmm": ([vp, i32, vp], ctypes.c_int),
         "sc_batch_free": ([vp], None),
+        "sc_graph_capture_plan": ([vp, vp, i64, vp, i64, i32, i32, P(vp)], ctypes.c_int),
+        "sc_graph_capture_batch": ([vp, i32, i32, P(vp)], ctypes.c_int),
+        "sc_graph_launch": ([vp, vp], ctypes.c_int),
+        "sc_graph_free": ([vp], None),
         "sc_spmm_dense_noalloc": ([vp, i64, i64, i64, vp, i64, i64, vp, i64, i32, vp], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
@@ -402,6 +407,14 @@ class SpMMPlan:
                                    len(flag_ptrs), int(epoch), 1 if accumulate else 0, self._stream(stream)))
         return C
 
+    def capture(self, B, C, repeat: int = 1, accumulate: bool = False) -> "Graph":
+        """CUDA graph of `repeat` products C = A @ B with these fixed tensors."""
+        h = ctypes.c_void_p()
+        _check(lib().sc_graph_capture_plan(self._h, ctypes.c_void_p(B.data_ptr()), B.stride(0),
+                                           ctypes.c_void_p(C.data_ptr()), C.stride(0), 1 if accumulate else 0,
+                                           repeat, ctypes.byref(h)))
+        return Graph(h.value, self.device, keep=(self, B, C))
+
     def spmv(self, x, y=None, accumulate: bool = False, stream=None):
         torch = _torch()
         if x.dtype != torch.float32 or not x.is_cuda or x.numel() != self.cols or not x.is_contiguous():
@@ -469,7 +482,32 @@ class SpMMBatch:
         _check(lib().sc_batch_spmm(self._h, 1 if accumulate else 0, ctypes.c_void_p(s.cuda_stream)))
         return self._bound[1] if self._bound else None
 
+    def capture(self, repeat: int = 1, accumulate: bool = False) -> "Graph":
+        """CUDA graph of `repeat` batch products with the bound operands."""
+        h = ctypes.c_void_p()
+        _check(lib().sc_graph_capture_batch(self._h, 1 if accumulate else 0, repeat, ctypes.byref(h)))
+        return Graph(h.value, self.plans[0].device, keep=(self,))
+
     def __del__(self):
         if getattr(self, "_h", None) and self._h.value and _lib is not None:
             _lib.sc_batch_free(self._h)
+            self._h = ctypes.c_void_p()
+
+
+class Graph:
+    """A captured CUDA graph of products (sc_graph); launch() replays it on a stream."""
+
+    def __init__(self, handle: int, device: int, keep=()):
+        self._h = ctypes.c_void_p(handle)
+        self.device = device
+        self._keep = keep  # the plan/batch and tensors the graph reads and writes
+
+    def launch(self, stream=None):
+        torch = _torch()
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        _check(lib().sc_graph_launch(self._h, ctypes.c_void_p(s.cuda_stream)))
+
+    def __del__(self):
+        if getattr(self, "_h", None) and self._h.value and _lib is not None:
+            _lib.sc_graph_free(self._h)
             self._h = ctypes.c_void_p()

@@ -888,3 +888,81 @@ int sc_batch_spmm(sc_batch *b, int32_t accumulate, void *stream) {
 void sc_batch_free(sc_batch *b) { delete b; }
 
 }  // extern "C"
+
+// A captured CUDA graph of `repeat` back-to-back products with fixed operands.
+struct sc_graph {
+  int device = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  ~sc_graph() {
+    int prev;
+    bool ok = cudaGetDevice(&prev) == cudaSuccess;
+    if (ok && prev != device) cudaSetDevice(device);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (ok && prev != device) cudaSetDevice(prev);
+  }
+};
+
+namespace {
+
+template <typename F>
+sc_graph *capture(int device, int repeat, F issue) {
+  require(repeat >= 1 && repeat <= 100000, SC_ERR_ARG, "repeat must be 1..100000");
+  DeviceGuard dg(device);
+  auto g = std::make_unique<sc_graph>();
+  g->device = device;
+  cudaStream_t s;
+  cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "create capture stream");
+  cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+  if (e == cudaSuccess) {
+    try {
+      for (int r = 0; r < repeat; ++r) issue(s);
+    } catch (...) {
+      cudaGraph_t junk = nullptr;
+      cudaStreamEndCapture(s, &junk);
+      if (junk) cudaGraphDestroy(junk);
+      cudaStreamDestroy(s);
+      throw;
+    }
+    e = cudaStreamEndCapture(s, &g->graph);
+  }
+  cudaStreamDestroy(s);
+  cuda_check(e, "stream capture");
+  cuda_check(cudaGraphInstantiate(&g->exec, g->graph, 0), "graph instantiate");
+  return g.release();
+}
+
+}  // namespace
+
+extern "C" {
+
+int sc_graph_capture_plan(sc_plan *p, const float *dB, int64_t ldb, float *dC, int64_t ldc, int32_t accumulate,
+                          int32_t repeat, sc_graph **out) {
+  SC_API_BEGIN
+  require(p != nullptr && out != nullptr, SC_ERR_ARG, "null argument");
+  *out = capture(p->device, repeat, [&](cudaStream_t s) { launch(p, dB, ldb, dC, ldc, accumulate, s); });
+  SC_API_END
+}
+
+int sc_graph_capture_batch(sc_batch *b, int32_t accumulate, int32_t repeat, sc_graph **out) {
+  SC_API_BEGIN
+  require(b != nullptr && out != nullptr, SC_ERR_ARG, "null argument");
+  *out = capture(b->device, repeat, [&](cudaStream_t s) {
+    int st = sc_batch_spmm(b, accumulate, s);
+    if (st != SC_OK) throw sc_error(st, sc_last_error_string());
+  });
+  SC_API_END
+}
+
+int sc_graph_launch(sc_graph *g, void *stream) {
+  SC_API_BEGIN
+  require(g != nullptr, SC_ERR_ARG, "null graph");
+  DeviceGuard dg(g->device);
+  cuda_check(cudaGraphLaunch(g->exec, static_cast<cudaStream_t>(stream)), "graph launch");
+  SC_API_END
+}
+
+void sc_graph_free(sc_graph *g) { delete g; }
+
+}  // extern "C"

@@ -309,3 +309,39 @@ def test_batch_mixed_dense_and_wide(cuda, monkeypatch):
     torch.cuda.synchronize()
     for (name, a, B), C in zip(mats, Cs):
         assert_parity(C.cpu().numpy(), a, B)
+
+
+@pytest.mark.parametrize("cfg", ["narrow", "wide", "dense"])
+def test_graph_capture_plan(cuda, monkeypatch, cfg):
+    import torch
+    if cfg == "narrow":
+        a, B = wl.config2(0.9, 4)
+    else:
+        monkeypatch.setenv("SC_DENSE", "1" if cfg == "dense" else "0")
+        a, B = wl.config3((2048, 512), 128)
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+    plan = sc.SpMMPlan(cf, B.shape[1])
+    Bt = torch.from_numpy(B).to(cuda)
+    C = torch.zeros((a[0], B.shape[1]), device=cuda)
+    g = plan.capture(Bt, C, repeat=3, accumulate=True)  # three C += A*B per replay
+    for _ in range(2):
+        g.launch()
+    torch.cuda.synchronize()
+    assert_parity(C.cpu().numpy() / 6.0, a, B)
+
+
+def test_graph_capture_batch(cuda):
+    import torch
+    mats = wl.config4(128)[:10]
+    plans, Bs, Cs = [], [], []
+    for name, a, B in mats:
+        plans.append(sc.SpMMPlan(sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1), 128))
+        Bs.append(torch.from_numpy(B).to(cuda))
+        Cs.append(torch.full((a[0], 128), float("nan"), device=cuda))
+    batch = sc.SpMMBatch(plans)
+    batch.bind(Bs, Cs)
+    g = batch.capture(repeat=4)
+    g.launch()
+    torch.cuda.synchronize()
+    for (name, a, B), C in zip(mats, Cs):
+        assert_parity(C.cpu().numpy(), a, B)
