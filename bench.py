@@ -57,6 +57,9 @@ def parse():
                    help="N>1 row partition: C blocks stored to peers by the SpMM kernel itself over NVLink "
                         "(symmetric memory) and completion flags (peer) or a barrier (peer-barrier), or "
                         "gathered afterwards with NCCL all-gather (nccl)")
+    p.add_argument("--dense-bf16", action="store_true",
+                   help="opt-in: dense-tile plans on bf16 tiles (fp32 accumulation, looser error bound) "
+                        "instead of 3xTF32; the default and the reference compute in fp32")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU work of the bounded cpu_baseline sample")
     return p.parse_args()
@@ -432,6 +435,7 @@ def main():
             tuned[i] = tuning.autotune_kernel_m(sc.CSR.from_arrays(*a), N, device=local)[0]
         return tuned[i]
 
+    plan_flags = sc.SC_PLAN_DENSE_BF16 if args.dense_bf16 else 0
     if layers:
         owner = lpt_assign([len(a[3]) for a, _ in mats], world)
         mine = [i for i, r in enumerate(owner) if r == rank]
@@ -439,7 +443,7 @@ def main():
             a, B = mats[i]
             mk = pick_m(i, a)
             cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*a), mk, kn)
-            plan = sc.SpMMPlan(cf, N, device=local)
+            plan = sc.SpMMPlan(cf, N, device=local, flags=plan_flags)
             jobs.append({"km": mk, "plan": plan, "B": torch.from_numpy(B).to(dev), "rows": a[0], "max_rows": a[0],
                          "m": a[0], "nnz_local": len(a[3]), "Bhost": B, "cuts": None, "K": a[1],
                          "C": torch.empty((a[0], N), device=dev)})
@@ -452,7 +456,7 @@ def main():
             r0, r1 = min(p0 * mk, m), min(p1 * mk, m)
             blk = row_slice(a, r0, r1)
             cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*blk), mk, kn)
-            plan = sc.SpMMPlan(cf, N, device=local)
+            plan = sc.SpMMPlan(cf, N, device=local, flags=plan_flags)
             max_rows = max(min(cuts[r + 1] * mk, m) - min(cuts[r] * mk, m) for r in range(world))
             j = {"km": mk, "plan": plan, "B": torch.from_numpy(B).to(dev), "rows": r1 - r0, "max_rows": max_rows,
                  "m": m, "nnz_local": len(blk[3]), "Bhost": B, "cuts": cuts, "K": a[1]}
@@ -636,7 +640,9 @@ def main():
     line = {
         "metric": "SpMM GFLOP/s (2*nnz*N)", "value": value, "unit": "GFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32" if not any(j["plan"].info["dense_bf16"] for j in jobs) else "bf16 tiles, f32 accumulate",
+        "data": "synthetic (seeded)",
         "config": {"workload": name,
                    "coarsening": ([km, kn] if not auto_m else
                                   {"kernel_m": "auto (measured per matrix)", "chosen": sorted({j["km"] for j in jobs}),

@@ -122,6 +122,23 @@ int sc_plan_create(const sc_cf *cf, int32_t n_cols_b, int32_t device, sc_plan **
 int sc_plan_create_panels(const sc_cf *cf, int32_t n_cols_b, int32_t device,
                           int64_t panel_begin, int64_t panel_end, sc_plan **out);
 
+/* sc_plan_create with options.  panel_begin = panel_end = -1 plans the whole
+ * matrix, otherwise as sc_plan_create_panels.  flags (OR of):
+ *   SC_PLAN_DENSE_OFF   never use the dense-tile tensor-core kernel;
+ *   SC_PLAN_DENSE_ON    use it whenever N is a multiple of 128, whatever the
+ *                       density (default: density >= 15 %);
+ *   SC_PLAN_DENSE_BF16  dense tiles in bf16 instead of 3xTF32: A and B are
+ *                       rounded to bf16 (8-bit mantissa), products accumulate
+ *                       in fp32; |C - A*B| <= 2^-7 * (|A|*|B|) elementwise
+ *                       instead of the fp32 bound.  Opt-in only; the
+ *                       reference computes in fp32.
+ * The flags override the SC_DENSE environment variable. */
+#define SC_PLAN_DENSE_OFF 1u
+#define SC_PLAN_DENSE_ON 2u
+#define SC_PLAN_DENSE_BF16 4u
+int sc_plan_create_ex(const sc_cf *cf, int32_t n_cols_b, int32_t device, int64_t panel_begin,
+                      int64_t panel_end, uint32_t flags, sc_plan **out);
+
 typedef struct sc_plan_info {
   int64_t rows;          /* C rows this plan produces */
   int64_t cols;          /* K (rows of B) */
@@ -135,6 +152,8 @@ typedef struct sc_plan_info {
   int32_t kernel;        /* 1 = small-B (N<=4) kernel, 2 = large-B kernel,
                             3 = dense-tile tensor-core (tcgen05 3xTF32) kernel */
   int32_t warps_per_panel;
+  int32_t dense_bf16;    /* 1: the dense-tile kernel runs on bf16 tiles */
+  int32_t reserved;
 } sc_plan_info;
 int sc_plan_get_info(const sc_plan *p, sc_plan_info *info);
 

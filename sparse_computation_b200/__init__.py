@@ -41,6 +41,11 @@ SC_ERR_CUDA = 4
 SC_ERR_UNSUPPORTED = 5
 SC_ERR_NOMEM = 6
 
+# sc_plan_create_ex flags
+SC_PLAN_DENSE_OFF = 1
+SC_PLAN_DENSE_ON = 2
+SC_PLAN_DENSE_BF16 = 4
+
 # Every symbol include/sc_b200.h declares (checked by the CPU tests).
 EXPORTED_SYMBOLS = (
     "sc_version", "sc_last_error_string",
@@ -48,7 +53,7 @@ EXPORTED_SYMBOLS = (
     "sc_cf_load", "sc_cf_from_csr", "sc_cf_write", "sc_cf_dims", "sc_cf_header_line",
     "sc_cf_pattern_sizes", "sc_cf_pattern_arrays", "sc_cf_real_nnz", "sc_cf_free",
     "sc_companion_mtx_path", "sc_cf_write_binary", "sc_cf_load_binary",
-    "sc_plan_create", "sc_plan_create_panels", "sc_plan_get_info", "sc_spmm", "sc_spmv",
+    "sc_plan_create", "sc_plan_create_panels", "sc_plan_create_ex", "sc_plan_get_info", "sc_spmm", "sc_spmv",
     "sc_spmm_host", "sc_plan_free", "sc_spmm_peers", "sc_wait_flags",
     "sc_batch_create", "sc_batch_bind", "sc_batch_spmm", "sc_batch_free",
     "sc_spmm_dense_noalloc",
@@ -67,7 +72,8 @@ class ScError(RuntimeError):
 class _PlanInfo(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int64) for n in (
         "rows", "cols", "n_cols_b", "panels", "kernel_m", "nnz", "entries", "items",
-        "device_bytes")] + [("kernel", ctypes.c_int32), ("warps_per_panel", ctypes.c_int32)]
+        "device_bytes")] + [("kernel", ctypes.c_int32), ("warps_per_panel", ctypes.c_int32),
+                        ("dense_bf16", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 _lib = None
@@ -107,6 +113,7 @@ def lib() -> ctypes.CDLL:
         "sc_cf_load_binary": ([cp, P(vp)], ctypes.c_int),
         "sc_plan_create": ([vp, i32, i32, P(vp)], ctypes.c_int),
         "sc_plan_create_panels": ([vp, i32, i32, i64, i64, P(vp)], ctypes.c_int),
+        "sc_plan_create_ex": ([vp, i32, i32, i64, i64, ctypes.c_uint32, P(vp)], ctypes.c_int),
         "sc_plan_get_info": ([vp, P(_PlanInfo)], ctypes.c_int),
         "sc_spmm": ([vp, vp, i64, vp, i64, i32, vp], ctypes.c_int),
         "sc_spmv": ([vp, vp, vp, i32, vp], ctypes.c_int),
@@ -347,13 +354,18 @@ class SpMMPlan:
     ``spmm(B, C=None, accumulate=False)`` computes C = A @ B (or C += A @ B)
     for float32 CUDA tensors B (K x N) and C (rows x N), row-major with unit
     column stride, on torch's current stream of the plan's device.
+    ``flags`` (SC_PLAN_DENSE_OFF / _ON / _BF16) select the dense-tile kernel and
+    its precision; bf16 tiles are opt-in and carry a looser error bound.
     """
 
     def __init__(self, cf: CompressedFormat, n_cols_b: int, device: int = 0,
-                 panel_range: Optional[Tuple[int, int]] = None):
+                 panel_range: Optional[Tuple[int, int]] = None, flags: int = 0):
         self.cf = cf
         h = ctypes.c_void_p()
-        if panel_range is None:
+        if flags:
+            pb, pe = panel_range if panel_range is not None else (-1, -1)
+            _check(lib().sc_plan_create_ex(cf._h, n_cols_b, device, pb, pe, flags, ctypes.byref(h)))
+        elif panel_range is None:
             _check(lib().sc_plan_create(cf._h, n_cols_b, device, ctypes.byref(h)))
         else:
             _check(lib().sc_plan_create_panels(cf._h, n_cols_b, device, panel_range[0], panel_range[1],

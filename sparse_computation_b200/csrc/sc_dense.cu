@@ -90,6 +90,19 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64
       : "memory");
 }
 
+// Instruction descriptor: D f32, A/B bf16 (kind::f16), both K-major, N=128, M=128.
+constexpr uint32_t kIdescBf16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                                ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdescBf16), "r"(accum)
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -119,14 +132,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // TMEM rows (C rows 32w..32w+31 of the tile) are owned by CTA w / (4/S); the
 // other CTAs send theirs into the owner's shared memory (slots of 32 rows x
 // 128 floats), then the owner adds them up and stores C.
-template <bool BATCH>
+template <bool BATCH, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
 dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *__restrict__ tasks, int accumulate,
                   int *status) {
+  // tf32 x3: stage = A_hi, A_lo, B_hi, B_lo (64 KiB), 3 stages;
+  // bf16:    stage = A, B (32 KiB), 6 stages.
+  constexpr int NST = BF16 ? 6 : kStages;
+  constexpr int SB = BF16 ? 2 * kTileBytes : kStageBytes;
   extern __shared__ __align__(1024) uint8_t dsmem[];
   // 1024-byte aligned stage ring (the swizzle is applied on address bits).
   uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages], done_bar;
+  __shared__ __align__(8) uint64_t full_bar[NST], empty_bar[NST], done_bar;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -145,7 +162,7 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
   const int nk = (c1 - c0 > crank) ? (c1 - c0 - crank + S - 1) / S : 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
@@ -165,43 +182,53 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
 
   if (threadIdx.x == 0 && nk > 0) {
     // producer
+    constexpr int OP = BF16 ? kTileBytes : 2 * kTileBytes;  // bytes of one operand's images
     for (int i = 0; i < nk; ++i) {
-      const int s = i % kStages;
-      if (i >= kStages && !mbar_wait(&empty_bar[s], ((i / kStages) - 1) & 1, &abort_flag)) {
+      const int s = i % NST;
+      if (i >= NST && !mbar_wait(&empty_bar[s], ((i / NST) - 1) & 1, &abort_flag)) {
         atomicExch(status, 1);
         abort_flag = 1;
         break;
       }
       const int ci = c0 + crank + i * S;
-      uint8_t *st = ring + (size_t)s * kStageBytes;
-      const uint8_t *at = m.a_tiles + (size_t)ci * 2 * kTileBytes;
+      uint8_t *st = ring + (size_t)s * SB;
+      const uint8_t *at = m.a_tiles + (size_t)ci * OP;
       const int kc = m.rb_chunk[ci];
-      const uint8_t *bt = m.b_tiles + ((size_t)nt * m.k_chunks + kc) * 2 * kTileBytes;
-      mbar_expect_tx(&full_bar[s], kStageBytes);
-      bulk_copy(st, at, 2 * kTileBytes, &full_bar[s]);
-      bulk_copy(st + 2 * kTileBytes, bt, 2 * kTileBytes, &full_bar[s]);
+      const uint8_t *bt = m.b_tiles + ((size_t)nt * m.k_chunks + kc) * OP;
+      mbar_expect_tx(&full_bar[s], SB);
+      bulk_copy(st, at, OP, &full_bar[s]);
+      bulk_copy(st + OP, bt, OP, &full_bar[s]);
     }
   } else if (threadIdx.x == 32 && nk > 0) {
     // MMA issuer
     bool ok = true;
     for (int i = 0; i < nk; ++i) {
-      const int s = i % kStages;
-      if (!mbar_wait(&full_bar[s], (i / kStages) & 1, &abort_flag)) {
+      const int s = i % NST;
+      if (!mbar_wait(&full_bar[s], (i / NST) & 1, &abort_flag)) {
         atomicExch(status, 2);
         abort_flag = 1;
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t base = smem_u32(ring + (size_t)s * kStageBytes);
-      const uint64_t a_hi = sdesc(base), a_lo = sdesc(base + kTileBytes);
-      const uint64_t b_hi = sdesc(base + 2 * kTileBytes), b_lo = sdesc(base + 3 * kTileBytes);
+      const uint32_t base = smem_u32(ring + (size_t)s * SB);
+      if constexpr (BF16) {
+        const uint64_t a = sdesc(base), b = sdesc(base + kTileBytes);
 #pragma unroll
-      for (int k = 0; k < kBK / 8; ++k) {
-        const uint64_t step = (uint64_t)((k * 32) >> 4);  // 8 tf32 = 32 bytes along K
-        mma_tf32(tmem, a_lo + step, b_hi + step, (i > 0 || k > 0) ? 1u : 0u);
-        mma_tf32(tmem, a_hi + step, b_lo + step, 1u);
-        mma_tf32(tmem, a_hi + step, b_hi + step, 1u);
+        for (int k = 0; k < kBKb / 16; ++k) {
+          const uint64_t step = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
+          mma_bf16(tmem, a + step, b + step, (i > 0 || k > 0) ? 1u : 0u);
+        }
+      } else {
+        const uint64_t a_hi = sdesc(base), a_lo = sdesc(base + kTileBytes);
+        const uint64_t b_hi = sdesc(base + 2 * kTileBytes), b_lo = sdesc(base + 3 * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < kBK / 8; ++k) {
+          const uint64_t step = (uint64_t)((k * 32) >> 4);  // 8 tf32 = 32 bytes along K
+          mma_tf32(tmem, a_lo + step, b_hi + step, (i > 0 || k > 0) ? 1u : 0u);
+          mma_tf32(tmem, a_hi + step, b_lo + step, 1u);
+          mma_tf32(tmem, a_hi + step, b_hi + step, 1u);
+        }
       }
       mma_commit(&empty_bar[s]);  // stage free once these MMAs have read it
     }
@@ -323,29 +350,65 @@ __global__ void __launch_bounds__(256) split_b_kernel(DenseMat one, const DenseM
   }
 }
 
+// bf16 mode: one image per (n tile, 64-wide K chunk).
+template <bool BATCH>
+__global__ void __launch_bounds__(256) split_b_bf16_kernel(DenseMat one, const DenseMat *__restrict__ mats) {
+  __shared__ float T[kBKb][kBN + 1];
+  DenseMat m;
+  if constexpr (BATCH) m = mats[blockIdx.y];
+  else m = one;
+  const int tile = blockIdx.x;
+  if (tile >= m.n_tiles * m.k_chunks) return;
+  const int nt = tile / m.k_chunks, kc = tile % m.k_chunks;
+  for (int e = threadIdx.x; e < kBN * kBKb; e += blockDim.x) {
+    const int n = e % kBN, k = e / kBN;
+    const int gk = kc * kBKb + k, gn = nt * kBN + n;
+    T[k][n] = (gk < m.k_rows && gn < m.n_cols) ? __ldg(m.B + (int64_t)gk * m.ldb + gn) : 0.f;
+  }
+  __syncthreads();
+  uint4 *img = reinterpret_cast<uint4 *>(m.b_tiles + ((size_t)nt * m.k_chunks + kc) * kTileBytes);
+  // 16-byte chunk q: row n = q / 8, physical chunk c = q % 8 holding logical
+  // k = 8 * (c ^ (n & 7)) .. +7
+  for (int q = threadIdx.x; q < kBN * 8; q += blockDim.x) {
+    const int n = q >> 3, c = q & 7;
+    const int k0 = (c ^ (n & 7)) << 3;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w[j] = (uint32_t)bf16_bits(T[k0 + 2 * j][n]) | ((uint32_t)bf16_bits(T[k0 + 2 * j + 1][n]) << 16);
+    img[q] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 }  // namespace
 }  // namespace dense
 }  // namespace sc
 
 int sc_dense_split_b(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, int nmats, int max_tiles,
-                     cudaStream_t s) {
+                     bool bf16, cudaStream_t s) {
   using namespace sc::dense;
   if (nmats <= 0 || max_tiles <= 0) return 0;
-  if (mats) split_b_kernel<true><<<dim3(max_tiles, nmats), 256, 0, s>>>(one, mats);
-  else split_b_kernel<false><<<dim3(max_tiles, 1), 256, 0, s>>>(one, nullptr);
+  if (bf16) {
+    if (mats) split_b_bf16_kernel<true><<<dim3(max_tiles, nmats), 256, 0, s>>>(one, mats);
+    else split_b_bf16_kernel<false><<<dim3(max_tiles, 1), 256, 0, s>>>(one, nullptr);
+  } else {
+    if (mats) split_b_kernel<true><<<dim3(max_tiles, nmats), 256, 0, s>>>(one, mats);
+    else split_b_kernel<false><<<dim3(max_tiles, 1), 256, 0, s>>>(one, nullptr);
+  }
   return (int)cudaGetLastError();
 }
 
 int sc_dense_gemm(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, const int4 *tasks,
-                  int64_t ntasks, int split, int accumulate, int *status, cudaStream_t s) {
+                  int64_t ntasks, int split, bool bf16, int accumulate, int *status, cudaStream_t s) {
   using namespace sc::dense;
   if (ntasks <= 0) return 0;
   const size_t smem = (size_t)kStages * kStageBytes + 1024;
-  auto fn = mats ? dense_gemm_kernel<true> : dense_gemm_kernel<false>;
-  static unsigned attr_done[2] = {0, 0};  // one bit per device ordinal (< 32)
+  auto fn = mats ? (bf16 ? dense_gemm_kernel<true, true> : dense_gemm_kernel<true, false>)
+                 : (bf16 ? dense_gemm_kernel<false, true> : dense_gemm_kernel<false, false>);
+  static unsigned attr_done[4] = {0, 0, 0, 0};  // one bit per device ordinal (< 32)
   int dev = 0;
   cudaGetDevice(&dev);
-  unsigned &bits = attr_done[mats ? 1 : 0];
+  unsigned &bits = attr_done[(mats ? 1 : 0) + (bf16 ? 2 : 0)];
   if (dev >= 32 || !(bits & (1u << dev))) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;

@@ -55,6 +55,25 @@ __host__ __device__ inline float tf32_round(float x) {
   return y;
 }
 
+// BF16 mode (opt-in, looser tolerance): A and B tiles hold bf16 (round to
+// nearest even), one tcgen05.mma kind::f16 per 16-wide k-step, fp32
+// accumulation.  A tile row is still 128 bytes (64 bf16), so the tile image,
+// its swizzle and the per-k-step descriptor advance (32 bytes) are the same.
+constexpr int kBKb = 64;  // bf16 K per stage
+
+__host__ __device__ inline uint32_t swz_offset_bf16(int r, int k) {
+  const uint32_t chunk = (uint32_t)(k >> 3) ^ (uint32_t)(r & 7);
+  return (uint32_t)r * 128u + chunk * 16u + (uint32_t)(k & 7) * 2u;
+}
+
+__host__ __device__ inline uint16_t bf16_bits(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) return (uint16_t)((u >> 16) | ((u & 0xffffu) ? 0x40u : 0u));  // inf/nan
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
 // One matrix of the dense path.
 struct DenseMat {
   const uint8_t *a_tiles;   // per kept (row block, chunk): [hi image | lo image]
@@ -68,8 +87,9 @@ struct DenseMat {
   int64_t rows;             // C rows
   int k_rows;               // K
   int n_cols;               // N (multiple of 128)
-  int k_chunks;             // ceil(K / 32)
+  int k_chunks;             // ceil(K / 32), or ceil(K / 64) in bf16 mode
   int n_tiles;              // N / 128
+  int bf16;                 // 1: bf16 tiles (one image per operand)
 };
 
 }  // namespace dense
@@ -79,6 +99,6 @@ struct DenseMat {
 // matrices (or nullptr with `one` used instead when nmats == 1); `tasks`
 // holds int4 {matrix, row block, n tile, kept chunks}, heaviest first.
 int sc_dense_split_b(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, int nmats, int max_tiles,
-                     cudaStream_t s);
+                     bool bf16, cudaStream_t s);
 int sc_dense_gemm(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, const int4 *tasks,
-                  int64_t ntasks, int split, int accumulate, int *status, cudaStream_t s);
+                  int64_t ntasks, int split, bool bf16, int accumulate, int *status, cudaStream_t s);

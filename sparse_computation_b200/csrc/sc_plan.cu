@@ -75,6 +75,8 @@ struct sc_plan {
   int4 *dense_tasks = nullptr;  // {0, row block, n tile, kept chunks}, heaviest first
   int64_t dense_ntasks = 0;
   int dense_split = 1;          // CTAs (cluster) per task
+  bool dense_bf16 = false;      // bf16 tiles (SC_PLAN_DENSE_BF16) instead of 3xTF32
+  uint32_t flags = 0;           // SC_PLAN_* given at creation
   ~sc_plan() {
     if (dev || stage_b || stage_c || a_tiles || chunk_order || side) {
       int prev;
@@ -195,17 +197,21 @@ sc::dense::DenseMat dense_mat(const sc_plan *p, const float *B, int64_t ldb, flo
   m.rows = p->rows;
   m.k_rows = (int)p->cols;
   m.n_cols = (int)p->n;
-  m.k_chunks = (int)((p->cols + sc::dense::kBK - 1) / sc::dense::kBK);
+  const int bk = p->dense_bf16 ? sc::dense::kBKb : sc::dense::kBK;
+  m.k_chunks = (int)((p->cols + bk - 1) / bk);
   m.n_tiles = (int)(p->n / sc::dense::kBN);
+  m.bf16 = p->dense_bf16 ? 1 : 0;
   return m;
 }
 
 bool use_dense(const sc_plan &p, const sc_cf &cf) {
   const char *e = getenv("SC_DENSE");
-  if (e && e[0] == '0') return false;
+  if (p.flags & SC_PLAN_DENSE_OFF) return false;
+  if (!(p.flags & SC_PLAN_DENSE_ON) && e && e[0] == '0') return false;
   if (p.n % sc::dense::kBN != 0) return false;
   const double cells = (double)p.rows * (double)p.cols;
   if (cells <= 0 || (double)p.rows * p.cols * 4.0 > 2e9) return false;
+  if (p.flags & SC_PLAN_DENSE_ON) return true;
   if (e && e[0] == '1') return true;
   return (double)p.nnz / cells >= 0.15;
 }
@@ -215,7 +221,10 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
   const int km = (int)p.km;
   const int64_t rows = p.rows, K = p.cols;
   const int64_t rbs = (rows + kBM - 1) / kBM;
-  const int kcs = (int)((K + kBK - 1) / kBK);
+  const bool bf = p.dense_bf16;
+  const int bk = bf ? kBKb : kBK;            // K per chunk (one 128-byte tile row)
+  const int images = bf ? 1 : 2;            // bf16: one image; tf32: head + tail
+  const int kcs = (int)((K + bk - 1) / bk);
   // densify this plan's rows
   std::vector<float> A((size_t)rbs * kBM * K, 0.f);
   for (int64_t lp = 0; lp < p.panels; ++lp) {
@@ -235,34 +244,40 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
         }
     }
   }
-  // kept (row block, chunk) pairs and their [hi | lo] swizzled images
+  // kept (row block, chunk) pairs and their swizzled images: [hi | lo] fp32
+  // TF32 pairs, or one bf16 image
   std::vector<int32_t> rb_ptr(rbs + 1, 0), rb_chunk;
   std::vector<uint8_t> tiles;
   for (int64_t b = 0; b < rbs; ++b) {
     for (int kc = 0; kc < kcs; ++kc) {
       bool any = false;
       for (int r = 0; r < kBM && !any; ++r)
-        for (int k = 0; k < kBK; ++k) {
-          const int64_t gk = (int64_t)kc * kBK + k;
+        for (int k = 0; k < bk; ++k) {
+          const int64_t gk = (int64_t)kc * bk + k;
           if (gk < K && A[(size_t)(b * kBM + r) * K + gk] != 0.f) { any = true; break; }
         }
       if (!any) continue;
       rb_chunk.push_back(kc);
       const size_t off = tiles.size();
-      tiles.resize(off + 2 * kTileBytes, 0);
+      tiles.resize(off + (size_t)images * kTileBytes, 0);
       for (int r = 0; r < kBM; ++r)
-        for (int k = 0; k < kBK; ++k) {
-          const int64_t gk = (int64_t)kc * kBK + k;
+        for (int k = 0; k < bk; ++k) {
+          const int64_t gk = (int64_t)kc * bk + k;
           const float x = gk < K ? A[(size_t)(b * kBM + r) * K + gk] : 0.f;
-          const float h = tf32_round(x), l = tf32_round(x - h);
-          memcpy(&tiles[off + swz_offset(r, k)], &h, 4);
-          memcpy(&tiles[off + kTileBytes + swz_offset(r, k)], &l, 4);
+          if (bf) {
+            const uint16_t h = bf16_bits(x);
+            memcpy(&tiles[off + swz_offset_bf16(r, k)], &h, 2);
+          } else {
+            const float h = tf32_round(x), l = tf32_round(x - h);
+            memcpy(&tiles[off + swz_offset(r, k)], &h, 4);
+            memcpy(&tiles[off + kTileBytes + swz_offset(r, k)], &l, 4);
+          }
         }
     }
     rb_ptr[b + 1] = (int32_t)rb_chunk.size();
   }
   const int nts = (int)(p.n / kBN);
-  const size_t b_bytes = (size_t)nts * kcs * 2 * kTileBytes;
+  const size_t b_bytes = (size_t)nts * kcs * images * kTileBytes;
   std::vector<int4> tasks;
   for (int64_t b = 0; b < rbs; ++b)
     for (int t = 0; t < nts; ++t) tasks.push_back(make_int4(0, (int)b, t, rb_ptr[b + 1] - rb_ptr[b]));
@@ -320,7 +335,7 @@ int wave_model_warps(int km, int vec, bool batch, int64_t units, double avg_item
   return best_w;
 }
 
-sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int64_t pe) {
+sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int64_t pe, uint32_t flags) {
   const int km = cf.kernel_m;
   require(km >= 1 && km <= 6, SC_ERR_UNSUPPORTED, "plans support kernel_m 1..6");
   require(n >= 1, SC_ERR_ARG, "n_cols_b must be >= 1");
@@ -353,6 +368,8 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
 
   auto plan = std::make_unique<sc_plan>();
   plan->device = device;
+  plan->flags = flags;
+  plan->dense_bf16 = (flags & SC_PLAN_DENSE_BF16) != 0;
   plan->km = km;
   plan->n = n;
   plan->cols = cf.num_cols;
@@ -523,9 +540,10 @@ void launch_panels(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ld
   const int nb = (int)p->n;
   if (p->kernel == 3 && ldc % 4 == 0 && aligned(C, 16)) {
     const sc::dense::DenseMat m = dense_mat(p, B, ldb, C, ldc);
-    int e = sc_dense_split_b(m, nullptr, 1, m.n_tiles * m.k_chunks, stream);
+    int e = sc_dense_split_b(m, nullptr, 1, m.n_tiles * m.k_chunks, p->dense_bf16, stream);
     cuda_check((cudaError_t)e, "B tile split launch");
-    e = sc_dense_gemm(m, nullptr, p->dense_tasks, p->dense_ntasks, p->dense_split, accumulate, p->status, stream);
+    e = sc_dense_gemm(m, nullptr, p->dense_tasks, p->dense_ntasks, p->dense_split, p->dense_bf16, accumulate,
+                      p->status, stream);
     cuda_check((cudaError_t)e, "dense tile kernel launch");
     return;
   }
@@ -571,7 +589,7 @@ extern "C" {
 int sc_plan_create(const sc_cf *cf, int32_t n_cols_b, int32_t device, sc_plan **out) {
   SC_API_BEGIN
   require(cf != nullptr && out != nullptr, SC_ERR_ARG, "null argument");
-  *out = build_plan(*cf, n_cols_b, device, 0, -1);
+  *out = build_plan(*cf, n_cols_b, device, 0, -1, 0);
   SC_API_END
 }
 
@@ -580,7 +598,21 @@ int sc_plan_create_panels(const sc_cf *cf, int32_t n_cols_b, int32_t device, int
   SC_API_BEGIN
   require(cf != nullptr && out != nullptr, SC_ERR_ARG, "null argument");
   require(panel_begin >= 0 && panel_end >= panel_begin, SC_ERR_ARG, "bad panel range");
-  *out = build_plan(*cf, n_cols_b, device, panel_begin, panel_end);
+  *out = build_plan(*cf, n_cols_b, device, panel_begin, panel_end, 0);
+  SC_API_END
+}
+
+int sc_plan_create_ex(const sc_cf *cf, int32_t n_cols_b, int32_t device, int64_t panel_begin, int64_t panel_end,
+                      uint32_t flags, sc_plan **out) {
+  SC_API_BEGIN
+  require(cf != nullptr && out != nullptr, SC_ERR_ARG, "null argument");
+  require(panel_begin == -1 ? panel_end == -1 : (panel_begin >= 0 && panel_end >= panel_begin), SC_ERR_ARG,
+          "bad panel range (both -1 for the whole matrix)");
+  require((flags & ~(uint32_t)(SC_PLAN_DENSE_OFF | SC_PLAN_DENSE_ON | SC_PLAN_DENSE_BF16)) == 0, SC_ERR_ARG,
+          "unknown plan flag");
+  require(!((flags & SC_PLAN_DENSE_OFF) && (flags & (SC_PLAN_DENSE_ON | SC_PLAN_DENSE_BF16))), SC_ERR_ARG,
+          "SC_PLAN_DENSE_OFF excludes the other dense flags");
+  *out = build_plan(*cf, n_cols_b, device, panel_begin == -1 ? 0 : panel_begin, panel_end, flags);
   SC_API_END
 }
 
@@ -598,6 +630,8 @@ int sc_plan_get_info(const sc_plan *p, sc_plan_info *info) {
   info->device_bytes = (int64_t)p->dev_bytes;
   info->kernel = p->kernel;
   info->warps_per_panel = p->warps;
+  info->dense_bf16 = p->kernel == 3 && p->dense_bf16 ? 1 : 0;
+  info->reserved = 0;
   SC_API_END
 }
 
@@ -722,6 +756,7 @@ struct sc_batch {
   int64_t tasks = 0;                     // wide group: (matrix, panel) tasks
   int64_t dense_ntasks = 0;
   int dense_split = 1, dense_max_tiles = 0;
+  bool dense_bf16 = false;  // all dense plans of a batch share one precision
   void *dev = nullptr;  // wide descs | wide order | dense mats | dense tasks | status
   sc::WideArgs *descs = nullptr;
   int2 *order = nullptr;
@@ -757,6 +792,11 @@ int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out) {
             "batches run wide-B plans (n_cols_b not in {1, 2, 4})");
     require(p->device == b->device && p->n == b->n, SC_ERR_UNSUPPORTED,
             "plans of a batch must share device and n_cols_b");
+    if (p->kernel == 3) {
+      if (b->dense_ids.empty()) b->dense_bf16 = p->dense_bf16;
+      require(p->dense_bf16 == b->dense_bf16, SC_ERR_UNSUPPORTED,
+              "dense-tile plans of a batch must share one precision (all bf16 or all 3xTF32)");
+    }
     b->plans.push_back(plans[i]);
     (p->kernel == 3 ? b->dense_ids : b->wide_ids).push_back(i);
   }
@@ -792,7 +832,8 @@ int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out) {
   for (size_t gi = 0; gi < b->dense_ids.size(); ++gi) {
     const sc_plan *p = plans[b->dense_ids[gi]];
     const int nts = (int)(p->n / sc::dense::kBN);
-    const int kcs = (int)((p->cols + sc::dense::kBK - 1) / sc::dense::kBK);
+    const int bk = p->dense_bf16 ? sc::dense::kBKb : sc::dense::kBK;
+    const int kcs = (int)((p->cols + bk - 1) / bk);
     b->dense_max_tiles = std::max(b->dense_max_tiles, nts * kcs);
     std::vector<int32_t> rbp(p->row_blocks + 1);
     DeviceGuard dgp(p->device);
@@ -870,9 +911,10 @@ int sc_batch_spmm(sc_batch *b, int32_t accumulate, void *stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (b->dense_ntasks > 0) {
     sc::dense::DenseMat none{};
-    int e = sc_dense_split_b(none, b->dmats, (int)b->dense_ids.size(), b->dense_max_tiles, s);
+    int e = sc_dense_split_b(none, b->dmats, (int)b->dense_ids.size(), b->dense_max_tiles, b->dense_bf16, s);
     cuda_check((cudaError_t)e, "B tile split launch");
-    e = sc_dense_gemm(none, b->dmats, b->dtasks, b->dense_ntasks, b->dense_split, accumulate, b->status, s);
+    e = sc_dense_gemm(none, b->dmats, b->dtasks, b->dense_ntasks, b->dense_split, b->dense_bf16, accumulate,
+                      b->status, s);
     cuda_check((cudaError_t)e, "dense tile kernel launch");
   }
   if (b->tasks > 0) {

@@ -72,6 +72,19 @@ def test_plan_rejects_bad_cf_before_device():
     assert e.value.code == sc.SC_ERR_UNSUPPORTED
 
 
+def test_plan_flags_validated_on_host():
+    """sc_plan_create_ex rejects unknown or contradictory flags and bad panel
+    ranges before any CUDA call."""
+    a = sc.CSR.from_arrays(4, 4, [0, 1, 1, 1, 1], [2], [1.0])
+    cf = sc.csr_to_compressed_format_converter(a, 2, 1)
+    for flags, rng in ((8, None), (sc.SC_PLAN_DENSE_OFF | sc.SC_PLAN_DENSE_BF16, None),
+                       (sc.SC_PLAN_DENSE_OFF | sc.SC_PLAN_DENSE_ON, None), (sc.SC_PLAN_DENSE_ON, (2, 1)),
+                       (sc.SC_PLAN_DENSE_ON, (-1, 3))):
+        with pytest.raises(sc.ScError) as e:
+            sc.SpMMPlan(cf, 128, panel_range=rng, flags=flags)
+        assert e.value.code == sc.SC_ERR_ARG
+
+
 def test_csr_create_validates():
     with pytest.raises(sc.ScError):
         sc.CSR.from_arrays(2, 2, [0, 2, 1], [0, 1], [1.0, 2.0])
