@@ -60,6 +60,9 @@ def parse():
     p.add_argument("--dense-bf16", action="store_true",
                    help="opt-in: dense-tile plans on bf16 tiles (fp32 accumulation, looser error bound) "
                         "instead of 3xTF32; the default and the reference compute in fp32")
+    p.add_argument("--values", choices=["f32", "f16", "bf16"], default="f32",
+                   help="opt-in: small-B / SpMV plans (N in {1,2,4}) with A's values stored in 16 bits "
+                        "(fp32 products and sums, looser error bound); the default and the reference use fp32")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU work of the bounded cpu_baseline sample")
     return p.parse_args()
@@ -332,7 +335,8 @@ def small_b_sweep(args):
             a, B = wl.config2(sp, N)
             m, n, ip, ix, dx = a
             cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(*a), args.kernel_m, args.kernel_n)
-            plan = sc.SpMMPlan(cf, N, device=0)
+            plan = sc.SpMMPlan(cf, N, device=0, flags={"f32": 0, "f16": sc.SC_PLAN_VALUES_F16,
+                                                       "bf16": sc.SC_PLAN_VALUES_BF16}[args.values])
             Bt = torch.from_numpy(B).to(dev)
             C = torch.empty((m, N), device=dev)
             ours = events_ms(lambda: plan.spmm(Bt, C, stream=stream), reps)
@@ -357,7 +361,8 @@ def small_b_sweep(args):
                          "graph_speedup_vs_cusparse": cus / graph})
     print(json.dumps({"metric": "SpMM GFLOP/s (2*nnz*N)", "unit": "GFLOP/s", "config": {
         "workload": "config2 sweep: A 512x512 magnitude-pruned N(0,0.05^2), B 512xN",
-        "coarsening": [args.kernel_m, args.kernel_n], "l2": "warm (L2-resident)"}, "sweep": rows}), flush=True)
+        "coarsening": [args.kernel_m, args.kernel_n], "values": args.values, "l2": "warm (L2-resident)"},
+        "sweep": rows}), flush=True)
 
 
 # ----------------------------------------------------------- reference ---
@@ -435,7 +440,8 @@ def main():
             tuned[i] = tuning.autotune_kernel_m(sc.CSR.from_arrays(*a), N, device=local)[0]
         return tuned[i]
 
-    plan_flags = sc.SC_PLAN_DENSE_BF16 if args.dense_bf16 else 0
+    plan_flags = (sc.SC_PLAN_DENSE_BF16 if args.dense_bf16 else 0) | \
+        {"f32": 0, "f16": sc.SC_PLAN_VALUES_F16, "bf16": sc.SC_PLAN_VALUES_BF16}[args.values]
     if layers:
         owner = lpt_assign([len(a[3]) for a, _ in mats], world)
         mine = [i for i, r in enumerate(owner) if r == rank]
@@ -641,7 +647,9 @@ def main():
         "metric": "SpMM GFLOP/s (2*nnz*N)", "value": value, "unit": "GFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None,
-        "dtype": "f32" if not any(j["plan"].info["dense_bf16"] for j in jobs) else "bf16 tiles, f32 accumulate",
+        "dtype": ("bf16 tiles, f32 accumulate" if any(j["plan"].info["dense_bf16"] for j in jobs) else
+                  {0: "f32", 1: "f16 values, f32 accumulate", 2: "bf16 values, f32 accumulate"}[
+                      max(j["plan"].info["value_type"] for j in jobs)]),
         "data": "synthetic (seeded)",
         "config": {"workload": name,
                    "coarsening": ([km, kn] if not auto_m else

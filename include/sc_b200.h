@@ -132,10 +132,21 @@ int sc_plan_create_panels(const sc_cf *cf, int32_t n_cols_b, int32_t device,
  *                       in fp32; |C - A*B| <= 2^-7 * (|A|*|B|) elementwise
  *                       instead of the fp32 bound.  Opt-in only; the
  *                       reference computes in fp32.
+ *   SC_PLAN_VALUES_F16  small-B / SpMV plans (n_cols_b 1, 2, 4; K <= 65536):
+ *   SC_PLAN_VALUES_BF16 A's values stored as fp16 (resp. bf16) with 16-bit
+ *                       column indices -- half the record bytes; products
+ *                       and sums in fp32.  Bound: the fp32 one plus the value
+ *                       rounding, 2^-11 (fp16; absolute 2^-25 below 2^-14)
+ *                       resp. 2^-8 (bf16) relative per value.  Mirrors the
+ *                       reference's half-precision small-B kernels
+ *                       (example_cuda/spmm_small_b_col_demo_gpu_utils.h:2987-5168).
+ *                       fp16 rejects values beyond +-65504.
  * The flags override the SC_DENSE environment variable. */
 #define SC_PLAN_DENSE_OFF 1u
 #define SC_PLAN_DENSE_ON 2u
 #define SC_PLAN_DENSE_BF16 4u
+#define SC_PLAN_VALUES_F16 8u
+#define SC_PLAN_VALUES_BF16 16u
 int sc_plan_create_ex(const sc_cf *cf, int32_t n_cols_b, int32_t device, int64_t panel_begin,
                       int64_t panel_end, uint32_t flags, sc_plan **out);
 
@@ -153,7 +164,7 @@ typedef struct sc_plan_info {
                             3 = dense-tile tensor-core (tcgen05 3xTF32) kernel */
   int32_t warps_per_panel;
   int32_t dense_bf16;    /* 1: the dense-tile kernel runs on bf16 tiles */
-  int32_t reserved;
+  int32_t value_type;    /* A's stored values: 0 fp32, 1 fp16, 2 bf16 */
 } sc_plan_info;
 int sc_plan_get_info(const sc_plan *p, sc_plan_info *info);
 

@@ -101,6 +101,21 @@ def spmm_csr_double(indptr, indices, data, B):
     return C
 
 
+def round_values_f16(data):
+    """float32 values rounded to IEEE binary16 (round to nearest even, subnormals
+    kept) and back: what a 16-bit value record stores.  Models the reference's
+    half-precision value arrays (example_cuda/spmm_small_b_col_demo_gpu_utils.h:2987-5168)."""
+    return np.asarray(data, np.float32).astype(np.float16).astype(np.float32)
+
+
+def round_values_bf16(data):
+    """float32 values rounded to bfloat16 (round to nearest even on the 16 dropped
+    mantissa bits; finite inputs) and back."""
+    u = np.ascontiguousarray(data, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
 # ---------------------------------------------- the reference's own code --
 
 def ref_available(name="libref_spmm.so") -> bool:

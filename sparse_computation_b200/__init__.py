@@ -45,6 +45,8 @@ SC_ERR_NOMEM = 6
 SC_PLAN_DENSE_OFF = 1
 SC_PLAN_DENSE_ON = 2
 SC_PLAN_DENSE_BF16 = 4
+SC_PLAN_VALUES_F16 = 8
+SC_PLAN_VALUES_BF16 = 16
 
 # Every symbol include/sc_b200.h declares (checked by the CPU tests).
 EXPORTED_SYMBOLS = (
@@ -73,7 +75,7 @@ class _PlanInfo(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int64) for n in (
         "rows", "cols", "n_cols_b", "panels", "kernel_m", "nnz", "entries", "items",
         "device_bytes")] + [("kernel", ctypes.c_int32), ("warps_per_panel", ctypes.c_int32),
-                        ("dense_bf16", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                        ("dense_bf16", ctypes.c_int32), ("value_type", ctypes.c_int32)]
 
 
 _lib = None
@@ -355,7 +357,8 @@ class SpMMPlan:
     for float32 CUDA tensors B (K x N) and C (rows x N), row-major with unit
     column stride, on torch's current stream of the plan's device.
     ``flags`` (SC_PLAN_DENSE_OFF / _ON / _BF16) select the dense-tile kernel and
-    its precision; bf16 tiles are opt-in and carry a looser error bound.
+    its precision; SC_PLAN_VALUES_F16 / _BF16 store A's values in 16 bits for
+    small-B / SpMV plans.  The 16-bit modes are opt-in, with looser error bounds.
     """
 
     def __init__(self, cf: CompressedFormat, n_cols_b: int, device: int = 0,

@@ -24,10 +24,16 @@ sc::WideFn SC_CAT(sc_wide_kernel_km, SC_KM)(int vec, bool batch) {
   }
 }
 
-sc::NarrowFn SC_CAT(sc_narrow_kernel_km, SC_KM)(int nb) {
+template <int VT>
+static sc::NarrowFn narrow_of(int nb) {
   switch (nb) {
-    case 1: return sc::spmm_narrow_kernel<SC_KM, 1>;
-    case 2: return sc::spmm_narrow_kernel<SC_KM, 2>;
-    default: return sc::spmm_narrow_kernel<SC_KM, 4>;
+    case 1: return sc::spmm_narrow_kernel<SC_KM, 1, VT>;
+    case 2: return sc::spmm_narrow_kernel<SC_KM, 2, VT>;
+    default: return sc::spmm_narrow_kernel<SC_KM, 4, VT>;
   }
+}
+
+// vt: 0 = fp32 records, 1 = fp16 compact records, 2 = bf16 compact records
+sc::NarrowFn SC_CAT(sc_narrow_kernel_km, SC_KM)(int nb, int vt) {
+  return vt == 1 ? narrow_of<1>(nb) : (vt == 2 ? narrow_of<2>(nb) : narrow_of<0>(nb));
 }

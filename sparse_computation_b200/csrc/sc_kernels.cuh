@@ -26,6 +26,8 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace sc {
@@ -105,6 +107,39 @@ __device__ __forceinline__ void load_rec(const uint32_t *__restrict__ r, int &co
     uint32_t w[7] = {a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
     for (int p = 0; p < P; ++p) v[p] = __uint_as_float(w[p]);
+  }
+}
+
+// Compact 16-bit records (small-B plans created with SC_PLAN_VALUES_F16 or
+// SC_PLAN_VALUES_BF16): the same record layout with 16-bit units --
+// [column (uint16), v_0 .. v_{P-1} (fp16 or bf16), zero fill], stride S
+// halfwords with the same S as above, so every record is half the bytes of
+// its fp32 form and is read with one 4-, 8- or 16-byte load.  Offsets in the
+// items count halfwords.  VT: 1 = fp16, 2 = bf16.
+template <int VT>
+__device__ __forceinline__ float half_bits_to_float(uint32_t h) {
+  if constexpr (VT == 1) return __half2float(__ushort_as_half((unsigned short)h));
+  else return __bfloat162float(__ushort_as_bfloat16((unsigned short)h));
+}
+
+template <int P, int VT>
+__device__ __forceinline__ void load_rec16(const uint16_t *__restrict__ r, int &col, float (&v)[P]) {
+  constexpr int S = rec_stride(P);
+  uint32_t w[4];
+  if constexpr (S == 2) {
+    w[0] = __ldg(reinterpret_cast<const uint32_t *>(r));
+  } else if constexpr (S == 4) {
+    uint2 t = __ldg(reinterpret_cast<const uint2 *>(r));
+    w[0] = t.x; w[1] = t.y;
+  } else {
+    uint4 t = __ldg(reinterpret_cast<const uint4 *>(r));
+    w[0] = t.x; w[1] = t.y; w[2] = t.z; w[3] = t.w;
+  }
+  col = (int)(w[0] & 0xffffu);
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    const int h = p + 1;  // halfword index within the record
+    v[p] = half_bits_to_float<VT>((h & 1) ? (w[h >> 1] >> 16) : (w[h >> 1] & 0xffffu));
   }
 }
 
@@ -382,8 +417,8 @@ static __global__ void wait_flags_kernel(const int *flags, int n, int epoch, int
 // shared memory produce the panel's KM x NB block.  This replaces the
 // reference's lane-packed segmented shuffle reduction
 // (code_gen/spmm_small_b_col/spmm_small_b_col_format_code_generator.py:212-323).
-template <int KM, int MASK, int NB>
-__device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ rec, int len,
+template <int KM, int MASK, int NB, int VT>
+__device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ recs, uint32_t off, int len,
                                            const float *__restrict__ B, int64_t ldb, int lane,
                                            float (&acc)[KM][NB]) {
   constexpr int P = popc_c(MASK);
@@ -391,7 +426,8 @@ __device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ rec, int
   if (lane < len) {
     int col;
     float v[P];
-    load_rec<P>(rec + lane * S, col, v);
+    if constexpr (VT == 0) load_rec<P>(recs + off + lane * S, col, v);
+    else load_rec16<P, VT>(reinterpret_cast<const uint16_t *>(recs) + off + lane * S, col, v);
     float b[NB];
     load_vec<NB>(B + (int64_t)col * ldb, b);
 #pragma unroll
@@ -401,16 +437,16 @@ __device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ rec, int
   }
 }
 
-template <int KM, int NB, int LO, int HI>
-__device__ __forceinline__ void dispatch_narrow(int mask, const uint32_t *__restrict__ rec, int len,
+template <int KM, int NB, int VT, int LO, int HI>
+__device__ __forceinline__ void dispatch_narrow(int mask, const uint32_t *__restrict__ recs, uint32_t off, int len,
                                                 const float *__restrict__ B, int64_t ldb, int lane,
                                                 float (&acc)[KM][NB]) {
   if constexpr (HI - LO == 1) {
-    seg_narrow<KM, LO, NB>(rec, len, B, ldb, lane, acc);
+    seg_narrow<KM, LO, NB, VT>(recs, off, len, B, ldb, lane, acc);
   } else {
     constexpr int MID = (LO + HI) / 2;
-    if (mask < MID) dispatch_narrow<KM, NB, LO, MID>(mask, rec, len, B, ldb, lane, acc);
-    else dispatch_narrow<KM, NB, MID, HI>(mask, rec, len, B, ldb, lane, acc);
+    if (mask < MID) dispatch_narrow<KM, NB, VT, LO, MID>(mask, recs, off, len, B, ldb, lane, acc);
+    else dispatch_narrow<KM, NB, VT, MID, HI>(mask, recs, off, len, B, ldb, lane, acc);
   }
 }
 
@@ -458,7 +494,7 @@ __device__ __forceinline__ int transpose_reduce_index(int lane) {
   return idx;
 }
 
-template <int KM, int NB>
+template <int KM, int NB, int VT>
 __global__ void __launch_bounds__(256)
 spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ items,
                    const int32_t *__restrict__ item_ptr, const int32_t *__restrict__ order,
@@ -481,8 +517,8 @@ spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ i
   const int it0 = item_ptr[panel], it1 = item_ptr[panel + 1];
   for (int it = it0 + warp; it < it1; it += nw) {
     const int2 item = __ldg(items + it);
-    dispatch_narrow<KM, NB, 1, (1 << KM)>(item.y & 0xffff, recs + (uint32_t)item.x, item.y >> 16, B,
-                                          ldb, lane, acc);
+    dispatch_narrow<KM, NB, VT, 1, (1 << KM)>(item.y & 0xffff, recs, (uint32_t)item.x, item.y >> 16, B, ldb,
+                                              lane, acc);
   }
 
   float v[V];
@@ -517,9 +553,9 @@ sc::WideFn sc_wide_kernel_km3(int vec, bool batch);
 sc::WideFn sc_wide_kernel_km4(int vec, bool batch);
 sc::WideFn sc_wide_kernel_km5(int vec, bool batch);
 sc::WideFn sc_wide_kernel_km6(int vec, bool batch);
-sc::NarrowFn sc_narrow_kernel_km1(int nb);
-sc::NarrowFn sc_narrow_kernel_km2(int nb);
-sc::NarrowFn sc_narrow_kernel_km3(int nb);
-sc::NarrowFn sc_narrow_kernel_km4(int nb);
-sc::NarrowFn sc_narrow_kernel_km5(int nb);
-sc::NarrowFn sc_narrow_kernel_km6(int nb);
+sc::NarrowFn sc_narrow_kernel_km1(int nb, int vt);
+sc::NarrowFn sc_narrow_kernel_km2(int nb, int vt);
+sc::NarrowFn sc_narrow_kernel_km3(int nb, int vt);
+sc::NarrowFn sc_narrow_kernel_km4(int nb, int vt);
+sc::NarrowFn sc_narrow_kernel_km5(int nb, int vt);
+sc::NarrowFn sc_narrow_kernel_km6(int nb, int vt);

@@ -7,6 +7,7 @@
 // contiguous allocation holding a flat record stream and a work list.
 
 #include <algorithm>
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -76,6 +77,7 @@ struct sc_plan {
   int64_t dense_ntasks = 0;
   int dense_split = 1;          // CTAs (cluster) per task
   bool dense_bf16 = false;      // bf16 tiles (SC_PLAN_DENSE_BF16) instead of 3xTF32
+  int value_type = 0;           // records: 0 fp32, 1 compact fp16, 2 compact bf16 (small-B plans)
   uint32_t flags = 0;           // SC_PLAN_* given at creation
   ~sc_plan() {
     if (dev || stage_b || stage_c || a_tiles || chunk_order || side) {
@@ -137,14 +139,14 @@ WideFn wide_kernel_raw(int km, int vec, bool batch) {
 }
 WideFn wide_kernel(int km, int vec, bool batch) { return with_carveout(wide_kernel_raw(km, vec, batch)); }
 
-NarrowFn narrow_kernel(int km, int nb) {
+NarrowFn narrow_kernel(int km, int nb, int vt) {
   switch (km) {
-    case 1: return sc_narrow_kernel_km1(nb);
-    case 2: return sc_narrow_kernel_km2(nb);
-    case 3: return sc_narrow_kernel_km3(nb);
-    case 4: return sc_narrow_kernel_km4(nb);
-    case 5: return sc_narrow_kernel_km5(nb);
-    default: return sc_narrow_kernel_km6(nb);
+    case 1: return sc_narrow_kernel_km1(nb, vt);
+    case 2: return sc_narrow_kernel_km2(nb, vt);
+    case 3: return sc_narrow_kernel_km3(nb, vt);
+    case 4: return sc_narrow_kernel_km4(nb, vt);
+    case 5: return sc_narrow_kernel_km5(nb, vt);
+    default: return sc_narrow_kernel_km6(nb, vt);
   }
 }
 
@@ -370,6 +372,13 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   plan->device = device;
   plan->flags = flags;
   plan->dense_bf16 = (flags & SC_PLAN_DENSE_BF16) != 0;
+  plan->value_type = (flags & SC_PLAN_VALUES_F16) ? 1 : ((flags & SC_PLAN_VALUES_BF16) ? 2 : 0);
+  const bool compact = plan->value_type != 0;
+  if (compact) {
+    require(n == 1 || n == 2 || n == 4, SC_ERR_UNSUPPORTED,
+            "16-bit value records are for the small-B / SpMV kernel (n_cols_b 1, 2 or 4)");
+    require(cf.num_cols <= 65536, SC_ERR_UNSUPPORTED, "16-bit value records need K <= 65536 (16-bit columns)");
+  }
   plan->km = km;
   plan->n = n;
   plan->cols = cf.num_cols;
@@ -377,6 +386,7 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   plan->rows = std::max<int64_t>(0, std::min<int64_t>(cf.num_rows, pe * km) - pb * km);
 
   std::vector<uint32_t> recs;
+  std::vector<uint16_t> recs16;  // compact form: recs16[i] encodes recs[i] (same indexing, halfwords)
   std::vector<int2> items;
   std::vector<int32_t> item_ptr(plan->panels + 1, 0);
   std::vector<int64_t> work(plan->panels, 0);
@@ -403,7 +413,9 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
         const int32_t col = pt.cb[j];
         require(col >= 0 && col < cf.num_cols, SC_ERR_FORMAT, "column index out of range in CF");
         if (seg_start < 0) {
-          while (recs.size() % 4) recs.push_back(0);  // 16-byte aligned segment
+          // 16-byte aligned segment (8 words when compact: 16 bytes of halfwords)
+          const size_t al = compact ? 8 : 4;
+          while (recs.size() % al) recs.push_back(0);
           seg_start = (int64_t)recs.size();
         }
         recs.push_back((uint32_t)col);
@@ -415,6 +427,21 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
           if (!pt.pad[(size_t)j * P + p]) plan->nnz++;
         }
         for (int p = 1 + P; p < S; ++p) recs.push_back(0);
+        if (compact) {
+          recs16.resize(recs.size() - S, 0);  // alignment fill
+          recs16.push_back((uint16_t)col);
+          for (int p = 0; p < P; ++p) {
+            const float v = pt.vals[(size_t)j * P + p];
+            if (plan->value_type == 1) {
+              require(std::fabs(v) <= 65504.f || v != v, SC_ERR_UNSUPPORTED,
+                      "value outside the fp16 range; use SC_PLAN_VALUES_BF16");
+              recs16.push_back(__half_as_ushort(__float2half_rn(v)));
+            } else {
+              recs16.push_back(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
+            }
+          }
+          for (int p = 1 + P; p < S; ++p) recs16.push_back(0);
+        }
         seg_len++;
         plan->entries++;
         work[lp] += P + 2;
@@ -427,6 +454,14 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   plan->items = (int64_t)items.size();
   while (recs.size() % 4) recs.push_back(0);
   if (recs.empty()) recs.assign(4, 0);
+  if (compact) {
+    recs16.resize(recs.size(), 0);
+    // upload the halfword stream in place of the fp32 one
+    recs.assign((recs16.size() + 1) / 2, 0);
+    memcpy(recs.data(), recs16.data(), recs16.size() * 2);
+    while (recs.size() % 4) recs.push_back(0);
+    std::vector<uint16_t>().swap(recs16);
+  }
 
   std::vector<int32_t> order(plan->panels);
   for (int64_t i = 0; i < plan->panels; ++i) order[i] = (int32_t)i;
@@ -547,8 +582,10 @@ void launch_panels(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ld
     cuda_check((cudaError_t)e, "dense tile kernel launch");
     return;
   }
+  require(p->value_type == 0 || (ldb % nb == 0 && aligned(B, 4 * nb)), SC_ERR_ARG,
+          "plans with 16-bit value records need B rows aligned to n_cols_b floats");
   if (p->kernel == 1 && ldb % nb == 0 && aligned(B, 4 * nb)) {
-    NarrowFn fn = narrow_kernel((int)p->km, nb);
+    NarrowFn fn = narrow_kernel((int)p->km, nb, p->value_type);
     fn<<<dim3((unsigned)count), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, order, B, ldb, C, ldc,
                                                        p->rows, accumulate);
   } else {
@@ -608,8 +645,11 @@ int sc_plan_create_ex(const sc_cf *cf, int32_t n_cols_b, int32_t device, int64_t
   require(cf != nullptr && out != nullptr, SC_ERR_ARG, "null argument");
   require(panel_begin == -1 ? panel_end == -1 : (panel_begin >= 0 && panel_end >= panel_begin), SC_ERR_ARG,
           "bad panel range (both -1 for the whole matrix)");
-  require((flags & ~(uint32_t)(SC_PLAN_DENSE_OFF | SC_PLAN_DENSE_ON | SC_PLAN_DENSE_BF16)) == 0, SC_ERR_ARG,
-          "unknown plan flag");
+  require((flags & ~(uint32_t)(SC_PLAN_DENSE_OFF | SC_PLAN_DENSE_ON | SC_PLAN_DENSE_BF16 | SC_PLAN_VALUES_F16 |
+                                SC_PLAN_VALUES_BF16)) == 0,
+          SC_ERR_ARG, "unknown plan flag");
+  require(!((flags & SC_PLAN_VALUES_F16) && (flags & SC_PLAN_VALUES_BF16)), SC_ERR_ARG,
+          "SC_PLAN_VALUES_F16 and SC_PLAN_VALUES_BF16 exclude each other");
   require(!((flags & SC_PLAN_DENSE_OFF) && (flags & (SC_PLAN_DENSE_ON | SC_PLAN_DENSE_BF16))), SC_ERR_ARG,
           "SC_PLAN_DENSE_OFF excludes the other dense flags");
   *out = build_plan(*cf, n_cols_b, device, panel_begin == -1 ? 0 : panel_begin, panel_end, flags);
@@ -631,7 +671,7 @@ int sc_plan_get_info(const sc_plan *p, sc_plan_info *info) {
   info->kernel = p->kernel;
   info->warps_per_panel = p->warps;
   info->dense_bf16 = p->kernel == 3 && p->dense_bf16 ? 1 : 0;
-  info->reserved = 0;
+  info->value_type = p->value_type;
   SC_API_END
 }
 

@@ -77,9 +77,9 @@ def test_plan_flags_validated_on_host():
     ranges before any CUDA call."""
     a = sc.CSR.from_arrays(4, 4, [0, 1, 1, 1, 1], [2], [1.0])
     cf = sc.csr_to_compressed_format_converter(a, 2, 1)
-    for flags, rng in ((8, None), (sc.SC_PLAN_DENSE_OFF | sc.SC_PLAN_DENSE_BF16, None),
+    for flags, rng in ((32, None), (sc.SC_PLAN_DENSE_OFF | sc.SC_PLAN_DENSE_BF16, None),
                        (sc.SC_PLAN_DENSE_OFF | sc.SC_PLAN_DENSE_ON, None), (sc.SC_PLAN_DENSE_ON, (2, 1)),
-                       (sc.SC_PLAN_DENSE_ON, (-1, 3))):
+                       (sc.SC_PLAN_DENSE_ON, (-1, 3)), (sc.SC_PLAN_VALUES_F16 | sc.SC_PLAN_VALUES_BF16, None)):
         with pytest.raises(sc.ScError) as e:
             sc.SpMMPlan(cf, 128, panel_range=rng, flags=flags)
         assert e.value.code == sc.SC_ERR_ARG
