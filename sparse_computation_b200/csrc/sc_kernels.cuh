@@ -8,7 +8,8 @@
 //             mask.  Coarsening padding (zero values, repeated column) is
 //             dropped.  Every segment starts on a 16-byte boundary.
 //   items     int2 {record offset in words, mask | len << 16}: up to 32
-//             consecutive entries of one (panel, pattern) segment.
+//             (wide kernel) or 128 (narrow kernel) consecutive entries of
+//             one (panel, pattern) segment.
 //   item_ptr  items of local panel i are [item_ptr[i], item_ptr[i+1]).
 //   order     CTA -> panel map, heaviest panels first.
 //
@@ -32,7 +33,13 @@
 
 namespace sc {
 
-constexpr int kItemEntries = 32;
+#ifndef SC_NARROW_PREFETCH
+#define SC_NARROW_PREFETCH 1
+#endif
+
+constexpr int kItemEntries = 32;        // wide kernel: entries per item
+constexpr int kNarrowUnroll = 4;        // narrow kernel: entries per lane per pass
+constexpr int kNarrowItemEntries = 32 * kNarrowUnroll;
 
 __host__ __device__ constexpr int popc_c(int x) {
   int c = 0;
@@ -120,27 +127,6 @@ template <int VT>
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
   if constexpr (VT == 1) return __half2float(__ushort_as_half((unsigned short)h));
   else return __bfloat162float(__ushort_as_bfloat16((unsigned short)h));
-}
-
-template <int P, int VT>
-__device__ __forceinline__ void load_rec16(const uint16_t *__restrict__ r, int &col, float (&v)[P]) {
-  constexpr int S = rec_stride(P);
-  uint32_t w[4];
-  if constexpr (S == 2) {
-    w[0] = __ldg(reinterpret_cast<const uint32_t *>(r));
-  } else if constexpr (S == 4) {
-    uint2 t = __ldg(reinterpret_cast<const uint2 *>(r));
-    w[0] = t.x; w[1] = t.y;
-  } else {
-    uint4 t = __ldg(reinterpret_cast<const uint4 *>(r));
-    w[0] = t.x; w[1] = t.y; w[2] = t.z; w[3] = t.w;
-  }
-  col = (int)(w[0] & 0xffffu);
-#pragma unroll
-  for (int p = 0; p < P; ++p) {
-    const int h = p + 1;  // halfword index within the record
-    v[p] = half_bits_to_float<VT>((h & 1) ? (w[h >> 1] >> 16) : (w[h >> 1] & 0xffffu));
-  }
 }
 
 // ------------------------------------------------------------ wide B ------
@@ -411,29 +397,75 @@ static __global__ void wait_flags_kernel(const int *flags, int n, int epoch, int
 }
 
 // ------------------------------------------------------------ narrow B ----
-// N in {1, 2, 4}: lane l takes entry l of an item (items hold <= 32
-// entries), multiplies the P values by the NB-wide B row, and keeps KM*NB
+// N in {1, 2, 4}: lane l takes entries l, l+32, ... of an item,
+// multiplies their P values by the NB-wide B rows, and keeps KM*NB
 // partial sums; a warp transpose-reduction then a cross-warp pass through
 // shared memory produce the panel's KM x NB block.  This replaces the
 // reference's lane-packed segmented shuffle reduction
 // (code_gen/spmm_small_b_col/spmm_small_b_col_format_code_generator.py:212-323).
+//
+// Items of the narrow kernel hold up to 128 entries: lane l takes entries
+// l, l+32, l+64, l+96 and issues all their record loads, then all their B
+// loads, before the FMAs -- four independent DRAM requests per lane in
+// flight, and the item's mask dispatch paid once per 128 entries.
+template <int P, int VT>
+__device__ __forceinline__ void load_rec_any(const uint32_t *__restrict__ recs, uint32_t off, int &col,
+                                             float (&v)[P]) {
+  constexpr int S = rec_stride(P);
+  if constexpr (VT == 0) {
+    load_rec<P>(recs + off, col, v);
+  } else {
+    const uint16_t *r = reinterpret_cast<const uint16_t *>(recs) + off;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if constexpr (S == 2) {
+      w[0] = __ldg(reinterpret_cast<const uint32_t *>(r));
+    } else if constexpr (S == 4) {
+      const uint2 t = __ldg(reinterpret_cast<const uint2 *>(r));
+      w[0] = t.x; w[1] = t.y;
+    } else {
+      const uint4 t = __ldg(reinterpret_cast<const uint4 *>(r));
+      w[0] = t.x; w[1] = t.y; w[2] = t.z; w[3] = t.w;
+    }
+    col = (int)(w[0] & 0xffffu);
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const int h = p + 1;  // halfword index within the record
+      v[p] = half_bits_to_float<VT>((h & 1) ? (w[h >> 1] >> 16) : (w[h >> 1] & 0xffffu));
+    }
+  }
+}
+
 template <int KM, int MASK, int NB, int VT>
 __device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ recs, uint32_t off, int len,
                                            const float *__restrict__ B, int64_t ldb, int lane,
                                            float (&acc)[KM][NB]) {
   constexpr int P = popc_c(MASK);
   constexpr int S = rec_stride(P);
-  if (lane < len) {
-    int col;
-    float v[P];
-    if constexpr (VT == 0) load_rec<P>(recs + off + lane * S, col, v);
-    else load_rec16<P, VT>(reinterpret_cast<const uint16_t *>(recs) + off + lane * S, col, v);
-    float b[NB];
-    load_vec<NB>(B + (int64_t)col * ldb, b);
+  constexpr int U = kNarrowUnroll;
+  for (int e0 = 0; e0 < len; e0 += 32 * U) {
+    int col[U];
+    float v[U][P];
 #pragma unroll
-    for (int p = 0; p < P; ++p)
+    for (int u = 0; u < U; ++u) {
+      const int e = e0 + u * 32 + lane;
+      if (e < len) {
+        load_rec_any<P, VT>(recs, off + (uint32_t)(e * S), col[u], v[u]);
+      } else {
+        col[u] = 0;  // row 0 of B, weight 0
 #pragma unroll
-      for (int q = 0; q < NB; ++q) acc[nth_row(MASK, p)][q] = fmaf(v[p], b[q], acc[nth_row(MASK, p)][q]);
+        for (int p = 0; p < P; ++p) v[u][p] = 0.f;
+      }
+    }
+    float b[U][NB];
+#pragma unroll
+    for (int u = 0; u < U; ++u) load_vec<NB>(B + (int64_t)col[u] * ldb, b[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int q = 0; q < NB; ++q)
+          acc[nth_row(MASK, p)][q] = fmaf(v[u][p], b[u][q], acc[nth_row(MASK, p)][q]);
   }
 }
 
@@ -515,10 +547,29 @@ spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ i
     for (int q = 0; q < NB; ++q) acc[k][q] = 0.f;
 
   const int it0 = item_ptr[panel], it1 = item_ptr[panel + 1];
-  for (int it = it0 + warp; it < it1; it += nw) {
-    const int2 item = __ldg(items + it);
-    dispatch_narrow<KM, NB, VT, 1, (1 << KM)>(item.y & 0xffff, recs, (uint32_t)item.x, item.y >> 16, B, ldb,
-                                              lane, acc);
+#if SC_NARROW_PREFETCH
+  // The panel's records are one contiguous range: ask the bulk-copy engine to
+  // pull all of it into L2 at once, so the warps' record loads below meet L2
+  // latency instead of a chain of DRAM round trips.
+  if (threadIdx.x == 0 && it1 > it0) {
+    const int2 f = __ldg(items + it0), l = __ldg(items + it1 - 1);
+    const int pl = __popc(l.y & 0xffff);
+    const uint32_t end = (uint32_t)l.x + (uint32_t)((l.y >> 16) * (pl == 1 ? 2 : (pl <= 3 ? 4 : 8)));
+    constexpr uint32_t unit = VT == 0 ? 4u : 2u;
+    const uint32_t b0 = ((uint32_t)f.x * unit) & ~15u, b1 = (end * unit + 15u) & ~15u;
+    const char *base = reinterpret_cast<const char *>(recs) + b0;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base), "r"(b1 - b0) : "memory");
+  }
+#endif
+  const int mine_total = it1 > it0 + warp ? (it1 - it0 - warp + nw - 1) / nw : 0;  // items it0+warp+j*nw
+  for (int base = 0; base < mine_total; base += 32) {
+    const int cnt = min(32, mine_total - base);
+    const int2 mine = lane < cnt ? __ldg(items + it0 + warp + (base + lane) * nw) : make_int2(0, 0);
+    for (int j = 0; j < cnt; ++j) {
+      const int2 item = make_int2(__shfl_sync(0xffffffffu, mine.x, j), __shfl_sync(0xffffffffu, mine.y, j));
+      dispatch_narrow<KM, NB, VT, 1, (1 << KM)>(item.y & 0xffff, recs, (uint32_t)item.x, item.y >> 16, B, ldb,
+                                                lane, acc);
+    }
   }
 
   float v[V];

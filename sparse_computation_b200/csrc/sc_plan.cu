@@ -385,6 +385,9 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   plan->panels = pe - pb;
   plan->rows = std::max<int64_t>(0, std::min<int64_t>(cf.num_rows, pe * km) - pb * km);
 
+  // entries per item: 32 for the wide kernel (one cp.async stage), 128 for the
+  // narrow kernel (four entries per lane)
+  const int64_t item_cap = (n == 1 || n == 2 || n == 4) ? sc::kNarrowItemEntries : sc::kItemEntries;
   std::vector<uint32_t> recs;
   std::vector<uint16_t> recs16;  // compact form: recs16[i] encodes recs[i] (same indexing, halfwords)
   std::vector<int2> items;
@@ -399,8 +402,8 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
       int64_t seg_start = -1;
       int64_t seg_len = 0;
       auto close_items = [&]() {
-        for (int64_t e = 0; e < seg_len; e += sc::kItemEntries) {
-          int len = (int)std::min<int64_t>(sc::kItemEntries, seg_len - e);
+        for (int64_t e = 0; e < seg_len; e += item_cap) {
+          int len = (int)std::min<int64_t>(item_cap, seg_len - e);
           int64_t off = seg_start + e * S;
           require(off < (int64_t)UINT32_MAX / 2, SC_ERR_UNSUPPORTED, "record stream exceeds 8 GiB");
           items.push_back(make_int2((int)off, rowbits[g] | (len << 16)));
@@ -582,12 +585,19 @@ void launch_panels(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ld
     cuda_check((cudaError_t)e, "dense tile kernel launch");
     return;
   }
-  require(p->value_type == 0 || (ldb % nb == 0 && aligned(B, 4 * nb)), SC_ERR_ARG,
-          "plans with 16-bit value records need B rows aligned to n_cols_b floats");
-  if (p->kernel == 1 && ldb % nb == 0 && aligned(B, 4 * nb)) {
-    NarrowFn fn = narrow_kernel((int)p->km, nb, p->value_type);
-    fn<<<dim3((unsigned)count), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, order, B, ldb, C, ldc,
-                                                       p->rows, accumulate);
+  if (p->kernel == 1) {
+    if (ldb % nb == 0 && aligned(B, 4 * nb)) {
+      NarrowFn fn = narrow_kernel((int)p->km, nb, p->value_type);
+      fn<<<dim3((unsigned)count), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, order, B, ldb, C, ldc,
+                                                         p->rows, accumulate);
+    } else {
+      // B rows not aligned for an nb-wide vector load: one single-column
+      // launch per column of B (scalar loads at any alignment)
+      NarrowFn fn = narrow_kernel((int)p->km, 1, p->value_type);
+      for (int q = 0; q < nb; ++q)
+        fn<<<dim3((unsigned)count), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, order, B + q, ldb,
+                                                           C + q, ldc, p->rows, accumulate);
+    }
   } else {
     int vec = p->kernel == 2 ? p->vec : 1;
     while (vec > 1 && !(p->n % vec == 0 && ldb % vec == 0 && ldc % vec == 0 && aligned(B, 4 * vec) &&
