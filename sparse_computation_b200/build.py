@@ -77,7 +77,9 @@ def build(verbose: bool = False, force: bool = False) -> str:
 
 
 APPS = {"spmm_demo_gpu": 0, "spmm_small_b_col_demo_gpu": 1, "spmv_demo_gpu": 2}
-BIN = os.path.join(PKG, "bin")
+# Executables beside the package's own library; a library built elsewhere
+# (SC_LIB, e.g. a variant with other compile flags) gets its own bin/ beside it.
+BIN = os.path.join(PKG, "bin") if os.path.dirname(LIB) == PKG else os.path.join(os.path.dirname(LIB), "bin")
 
 
 def build_apps(force: bool = False) -> None:
