@@ -202,7 +202,11 @@ int sc_spmv(sc_plan *p, const float *dx, float *dy, int32_t accumulate, void *st
 /* End-to-end product from HOST buffers: copies hB (K x N, dense row-major)
  * to the device, runs sc_spmm, copies C back to hC (rows x N), and
  * synchronizes `stream`.  Staging buffers are allocated on the first call and
- * kept by the plan. */
+ * kept by the plan.  When hC is page-locked host memory the device can
+ * address (cudaHostAlloc / cudaMallocHost, or registered and mapped), the
+ * kernel writes C into it directly while it computes; otherwise C is staged
+ * on the device and copied back in row chunks that overlap the remaining
+ * kernels. */
 int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream);
 void sc_plan_free(sc_plan *p);
 
