@@ -159,6 +159,28 @@ def test_host_entry_point(cuda):
         assert_parity(C, a, B)
 
 
+def test_host_entry_point_pinned_buffers(cuda):
+    """Page-locked host buffers take the direct path (the kernel stores C into
+    host memory; B copied as two concurrent halves); pageable ones the staged,
+    row-chunked path.  Both match the oracle, and each other."""
+    import torch
+    a, B = wl.config3((2048, 512), 128)
+    for km in (4, 1):
+        cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), km, 1)
+        plan = sc.SpMMPlan(cf, 128)
+        hB = torch.from_numpy(B).pin_memory()
+        hC = torch.full((2048, 128), float("nan")).pin_memory()
+        for _ in range(2):
+            plan.spmm_host(hB.numpy(), hC.numpy())
+            assert_parity(hC.numpy(), a, B)
+        assert np.array_equal(plan.spmm_host(B), hC.numpy())
+    a1, B1 = wl.config2(0.9, 4)  # small-B plan through the direct path
+    plan = sc.SpMMPlan(sc.csr_to_compressed_format_converter(to_csr_handle(a1), 4, 1), 4)
+    hC = torch.empty((512, 4)).pin_memory()
+    plan.spmm_host(torch.from_numpy(B1).pin_memory().numpy(), hC.numpy())
+    assert_parity(hC.numpy(), a1, B1)
+
+
 def test_edge_matrices(cuda):
     import torch
     cases = [np.zeros((7, 5), np.float32), np.array([[0, 1.5, 0, 2]], np.float32), np.eye(9, dtype=np.float32),
