@@ -65,6 +65,14 @@ struct sc_plan {
   std::vector<int64_t> chunk_off;  // kHostChunks + 1 offsets into chunk_order (= panel ranges)
   cudaStream_t side = nullptr;
   cudaEvent_t chunk_ev[kHostChunks] = {};
+  // K-split item lists (wide plans): half 0 holds the entries whose column is
+  // below ksplit, half 1 the rest, so the host entry point can start on the
+  // first rows of B while the second ones are still being copied.
+  int64_t ksplit = 0;                         // 0: no split lists
+  int2 *khalf_items[2] = {nullptr, nullptr};  // one allocation
+  int32_t *khalf_ptr[2] = {nullptr, nullptr};
+  cudaStream_t side2 = nullptr;
+  cudaEvent_t host_ev[5] = {};
   std::vector<int64_t> work;  // per local panel, for batch scheduling
   // Dense-tile tensor-core path (kernel == 3): swizzled A_hi/A_lo tiles of
   // the kept (row block, K-chunk) pairs, per-call B tile images, error word.
@@ -80,13 +88,17 @@ struct sc_plan {
   int value_type = 0;           // records: 0 fp32, 1 compact fp16, 2 compact bf16 (small-B plans)
   uint32_t flags = 0;           // SC_PLAN_* given at creation
   ~sc_plan() {
-    if (dev || stage_b || stage_c || a_tiles || chunk_order || side) {
+    if (dev || stage_b || stage_c || a_tiles || chunk_order || side || khalf_items[0] || side2) {
       int prev;
       bool ok = cudaGetDevice(&prev) == cudaSuccess;
       if (ok && prev != device) cudaSetDevice(device);
       if (dev) cudaFree(dev);
       if (a_tiles) cudaFree(a_tiles);  // one allocation: tiles | rb_ptr | rb_chunk | b_tiles | status
       if (chunk_order) cudaFree(chunk_order);
+      if (khalf_items[0]) cudaFree(khalf_items[0]);
+      for (auto &e : host_ev)
+        if (e) cudaEventDestroy(e);
+      if (side2) cudaStreamDestroy(side2);
       for (auto &e : chunk_ev)
         if (e) cudaEventDestroy(e);
       if (side) cudaStreamDestroy(side);
@@ -314,6 +326,64 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
   p.kernel = 3;
 }
 
+// K-split item lists for the host entry point.  Each item's entries are
+// split at the first column >= ksplit; the cut is moved down to keep the
+// second part's records 16-byte aligned (the wide kernel stages records in
+// 16-byte pieces), which only moves a few low-column entries into half 1 --
+// half 1 runs after all of B has arrived, so that is still correct.  Entries
+// of an item must be in increasing column order (the coarsener's merge order);
+// otherwise no split lists are built.
+void build_ksplit(sc_plan &p, const std::vector<uint32_t> &recs, const std::vector<int2> &items,
+                  const std::vector<int32_t> &item_ptr) {
+  const int64_t kc = (p.cols / 2) & ~(int64_t)63;
+  std::vector<int2> half[2];
+  std::vector<int32_t> hptr[2];
+  hptr[0].push_back(0);
+  hptr[1].push_back(0);
+  for (int64_t lp = 0; lp < p.panels; ++lp) {
+    for (int32_t it = item_ptr[lp]; it < item_ptr[lp + 1]; ++it) {
+      const int2 item = items[it];
+      const int mask = item.y & 0xffff, len = item.y >> 16;
+      const int S = sc::rec_stride(__builtin_popcount(mask));
+      int j = 0;
+      int64_t prev = -1;
+      for (int e = 0; e < len; ++e) {
+        const int64_t col = recs[(size_t)item.x + (size_t)e * S];
+        if (col < prev) return;  // not column-sorted: no split lists
+        prev = col;
+        if (col < kc) j = e + 1;
+      }
+      const int step = S == 2 ? 2 : 1;  // 16-byte aligned start of the second part
+      const int j0 = j - j % step;
+      if (j0 > 0) half[0].push_back(make_int2(item.x, mask | (j0 << 16)));
+      if (len - j0 > 0) half[1].push_back(make_int2(item.x + j0 * S, mask | ((len - j0) << 16)));
+    }
+    hptr[0].push_back((int32_t)half[0].size());
+    hptr[1].push_back((int32_t)half[1].size());
+  }
+  auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  size_t off[4], tot = 0;
+  for (int h = 0; h < 2; ++h) {
+    off[2 * h] = tot;
+    tot += al(std::max<size_t>(1, half[h].size()) * sizeof(int2));
+    off[2 * h + 1] = tot;
+    tot += al(hptr[h].size() * 4);
+  }
+  char *base = nullptr;
+  cuda_check(cudaMalloc(&base, tot), "cudaMalloc(K-split items)");
+  for (int h = 0; h < 2; ++h) {
+    p.khalf_items[h] = reinterpret_cast<int2 *>(base + off[2 * h]);
+    p.khalf_ptr[h] = reinterpret_cast<int32_t *>(base + off[2 * h + 1]);
+    if (!half[h].empty())
+      cuda_check(cudaMemcpy(p.khalf_items[h], half[h].data(), half[h].size() * sizeof(int2), cudaMemcpyHostToDevice),
+                 "upload K-split items");
+    cuda_check(cudaMemcpy(p.khalf_ptr[h], hptr[h].data(), hptr[h].size() * 4, cudaMemcpyHostToDevice),
+               "upload K-split items");
+  }
+  p.ksplit = kc;
+  p.dev_bytes += tot;
+}
+
 // Warps per CTA (<= max_w, powers of two) minimising waves(W) * (2 + items/W)
 // for `units` CTAs averaging `avg_items` work items each; the device must be
 // current.
@@ -521,6 +591,7 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
                           cudaMemcpyHostToDevice),
                "upload panel order");
   if (plan->kernel == 2 && plan->rows > 0 && use_dense(*plan, cf)) build_dense(*plan, cf, pb, rowbits);
+  if (plan->kernel == 2 && plan->cols >= 4096 && plan->panels > 0) build_ksplit(*plan, recs, items, item_ptr);
   if (plan->kernel != 3 && plan->panels >= sc_plan::kHostChunks) {
     // panels split into kHostChunks contiguous row ranges, heaviest first inside each
     std::vector<int32_t> co;
@@ -609,6 +680,35 @@ void launch_panels(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ld
     fn<<<dim3((unsigned)count, slices), threads, smem, stream>>>(wide_args(p, B, ldb, C, ldc), nullptr, order,
                                                                  accumulate);
   }
+  cuda_check(cudaGetLastError(), "kernel launch");
+}
+
+// SC_HOST_KSPLIT=0 turns the host entry point's K-split pipeline off.
+bool host_ksplit_enabled() {
+  static const bool v = [] {
+    const char *e = getenv("SC_HOST_KSPLIT");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
+// One half of a K-split wide product over all panels: half 0 writes
+// C = A[:, :ksplit] B[:ksplit]; half 1 adds A[:, ksplit:] B[ksplit:] to it and,
+// when `host_c` is given, stores the finished tiles there as well.
+void launch_khalf(sc_plan *p, int h, float *C, float *host_c, cudaStream_t stream) {
+  int vec = p->vec;
+  while (vec > 1 && p->n % vec != 0) vec >>= 1;
+  const int slices = (int)((p->n + 32 * vec - 1) / (32 * vec));
+  sc::WideArgs a = wide_args(p, p->stage_b, p->n, C, p->n);
+  a.items = p->khalf_items[h];
+  a.item_ptr = p->khalf_ptr[h];
+  if (host_c) {
+    a.npeers = 1;
+    a.peers[0] = host_c;
+  }
+  WideFn fn = wide_kernel((int)p->km, vec, false);
+  const size_t smem = sc::wide_smem_bytes(p->warps, (int)p->km, vec);
+  fn<<<dim3((unsigned)p->panels, slices), 32 * p->warps, smem, stream>>>(a, nullptr, p->order, h);
   cuda_check(cudaGetLastError(), "kernel launch");
 }
 
@@ -763,6 +863,57 @@ int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream) {
     cuda_check(cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking), "create side stream");
     for (auto &e : p->chunk_ev) cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "create event");
   }
+  // C in page-locked host memory that this device can address: the kernel
+  // stores C straight into it over the host link while it computes, so the
+  // device-to-host transfer overlaps the whole product instead of following it.
+  float *dC_host = nullptr;
+  if (cb) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, hC) == cudaSuccess && at.type == cudaMemoryTypeHost && at.devicePointer)
+      dC_host = static_cast<float *>(at.devicePointer);
+    else
+      cudaGetLastError();  // pageable memory: not an error, use the staged copy below
+  }
+  if (dC_host && p->kernel == 2 && p->ksplit > 0 && host_ksplit_enabled()) {
+    // K-split pipeline: B rows [0, ksplit) arrive first (two concurrent
+    // quarter copies), the half-0 product runs on them while rows
+    // [ksplit, K) are still being copied, then the half-1 product adds the
+    // rest and stores the finished C tiles into host memory as its second
+    // (peer) destination.
+    if (!p->side2) {
+      cuda_check(cudaStreamCreateWithFlags(&p->side2, cudaStreamNonBlocking), "create side stream");
+      for (auto &e : p->host_ev) cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "create event");
+    }
+    const size_t row = (size_t)p->n * sizeof(float);
+    const size_t k0 = (size_t)p->ksplit, K = (size_t)p->cols;
+    const size_t cut[5] = {0, k0 / 2 * row, k0 * row, (k0 + (K - k0) / 2) * row, K * row};
+    const char *hb = reinterpret_cast<const char *>(hB);
+    char *db = reinterpret_cast<char *>(p->stage_b);
+    auto copy = [&](int q, cudaStream_t st) {
+      if (cut[q + 1] > cut[q])
+        cuda_check(cudaMemcpyAsync(db + cut[q], hb + cut[q], cut[q + 1] - cut[q], cudaMemcpyHostToDevice, st),
+                   "copy B to device");
+    };
+    cudaEvent_t *ev = p->host_ev;
+    cuda_check(cudaEventRecord(ev[0], s), "record event");
+    cuda_check(cudaStreamWaitEvent(p->side, ev[0], 0), "wait event");
+    copy(0, s);
+    cuda_check(cudaEventRecord(ev[1], s), "record event");
+    copy(1, p->side);
+    cuda_check(cudaEventRecord(ev[2], p->side), "record event");
+    copy(2, p->side);
+    cuda_check(cudaEventRecord(ev[3], p->side), "record event");
+    cuda_check(cudaStreamWaitEvent(p->side2, ev[1], 0), "wait event");
+    copy(3, p->side2);
+    cuda_check(cudaEventRecord(ev[4], p->side2), "record event");
+    cuda_check(cudaStreamWaitEvent(s, ev[2], 0), "wait event");
+    launch_khalf(p, 0, p->stage_c, nullptr, s);
+    cuda_check(cudaStreamWaitEvent(s, ev[3], 0), "wait event");
+    cuda_check(cudaStreamWaitEvent(s, ev[4], 0), "wait event");
+    launch_khalf(p, 1, p->stage_c, dC_host, s);
+    cuda_check(cudaStreamSynchronize(s), "stream synchronize");
+    return SC_OK;
+  }
   if (bb >= (1u << 20)) {
     // two concurrent copies (this stream + the side stream): one DMA stream
     // alone does not fill the host link (measured 27-42 GB/s alone, 47 GB/s
@@ -778,17 +929,6 @@ int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream) {
     cuda_check(cudaStreamWaitEvent(s, p->chunk_ev[1], 0), "wait event");
   } else if (bb) {
     cuda_check(cudaMemcpyAsync(p->stage_b, hB, bb, cudaMemcpyHostToDevice, s), "copy B to device");
-  }
-  // C in page-locked host memory that this device can address: the kernel
-  // stores C straight into it over the host link while it computes, so the
-  // device-to-host transfer overlaps the whole product instead of following it.
-  float *dC_host = nullptr;
-  if (cb) {
-    cudaPointerAttributes at{};
-    if (cudaPointerGetAttributes(&at, hC) == cudaSuccess && at.type == cudaMemoryTypeHost && at.devicePointer)
-      dC_host = static_cast<float *>(at.devicePointer);
-    else
-      cudaGetLastError();  // pageable memory: not an error, use the staged copy below
   }
   if (dC_host) {
     launch(p, p->stage_b, p->n, dC_host, p->n, 0, s);
