@@ -697,7 +697,7 @@ bool host_ksplit_enabled() {
 // when `host_c` is given, stores the finished tiles there as well.
 void launch_khalf(sc_plan *p, int h, float *C, float *host_c, cudaStream_t stream) {
   int vec = p->vec;
-  while (vec > 1 && p->n % vec != 0) vec >>= 1;
+  while (vec > 1 && (p->n % vec != 0 || (host_c && !aligned(host_c, 4 * vec)))) vec >>= 1;
   const int slices = (int)((p->n + 32 * vec - 1) / (32 * vec));
   sc::WideArgs a = wide_args(p, p->stage_b, p->n, C, p->n);
   a.items = p->khalf_items[h];

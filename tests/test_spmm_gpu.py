@@ -174,6 +174,23 @@ def test_host_entry_point_pinned_buffers(cuda):
             plan.spmm_host(hB.numpy(), hC.numpy())
             assert_parity(hC.numpy(), a, B)
         assert np.array_equal(plan.spmm_host(B), hC.numpy())
+    # K >= 4096: the wide plan's K-split pipeline (half the columns per launch,
+    # second launch stores C to the host); odd item cuts included
+    a2 = wl.magnitude_pruned(1000, 6000, 0.95, 0.05, 77)
+    B2 = wl.dense_b(6000, 64, 78)
+    for km in (4, 3):
+        plan = sc.SpMMPlan(sc.csr_to_compressed_format_converter(to_csr_handle(a2), km, 1), 64)
+        hB = torch.from_numpy(B2).pin_memory()
+        hC = torch.full((1000, 64), float("nan")).pin_memory()
+        for _ in range(2):
+            plan.spmm_host(hB.numpy(), hC.numpy())
+            assert_parity(hC.numpy(), a2, B2)
+        assert_parity(plan.spmm_host(B2), a2, B2)
+    # a page-locked C that is only 4-byte aligned (narrower stores)
+    buf = torch.empty(1000 * 64 + 1).pin_memory()
+    hC = buf[1:].view(1000, 64)
+    plan.spmm_host(torch.from_numpy(B2).pin_memory().numpy(), hC.numpy())
+    assert_parity(hC.numpy(), a2, B2)
     a1, B1 = wl.config2(0.9, 4)  # small-B plan through the direct path
     plan = sc.SpMMPlan(sc.csr_to_compressed_format_converter(to_csr_handle(a1), 4, 1), 4)
     hC = torch.empty((512, 4)).pin_memory()
