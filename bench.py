@@ -430,6 +430,8 @@ def main():
 
     import sparse_computation_b200 as sc
 
+    sc.lib()  # builds libsc_b200.so in-tree when it is missing (ranks of one node build once)
+
     if args.sweep_small:
         small_b_sweep(args)
         return

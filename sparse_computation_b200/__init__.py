@@ -82,13 +82,20 @@ _lib = None
 
 
 def lib() -> ctypes.CDLL:
-    """Loads libsc_b200.so (built by ``sparse_computation_b200.build``)."""
+    """Loads libsc_b200.so, building it in-tree first (about a minute with
+    nvcc, ``sparse_computation_b200.build``) when it is missing.  There is no
+    fallback: without nvcc and without a built library this raises."""
     global _lib
     if _lib is not None:
         return _lib
     if not os.path.exists(LIB_PATH):
-        raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m sparse_computation_b200.build`")
+        from . import build as _build
+        try:
+            _build.build()
+        except Exception as ex:
+            raise ImportError(f"{LIB_PATH} is missing and could not be built: {ex}") from ex
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing after the build")
     L = ctypes.CDLL(LIB_PATH)
     P = ctypes.POINTER
     vp = ctypes.c_void_p

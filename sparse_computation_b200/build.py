@@ -26,10 +26,12 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CXXFLAGS = ["-O3", "-std=c++17", "-fPIC", "-pthread", "-Wall", "-Wno-unused-function"]
 
 HOST_SOURCES = ["sc_host.cpp"]
-# (source, extra flags, object name): sc_inst.cu is compiled once per kernel_m.
+# (source, extra flags, object name): sc_inst.cu is compiled once per
+# (kernel_m, wide|narrow); the slowest units are listed first.
 CUDA_SOURCES = [("sc_plan.cu", [], "sc_plan.cu.o"), ("sc_dense.cu", [], "sc_dense.cu.o"),
                 ("sc_noalloc.cu", [], "sc_noalloc.cu.o")] + [
-    ("sc_inst.cu", [f"-DSC_KM={km}"], f"sc_inst_km{km}.cu.o") for km in range(1, 7)]
+    ("sc_inst.cu", [f"-DSC_KM={km}", f"-DSC_PART={part}"], f"sc_inst_km{km}_{'wn'[part]}.cu.o")
+    for km in (4, 6, 5, 3, 2, 1) for part in (0, 1)]
 
 
 def _run(cmd):
@@ -47,7 +49,19 @@ def _newer(target, deps):
 
 
 def build(verbose: bool = False, force: bool = False) -> str:
+    """Compiles what is missing or stale.  Serialised across processes by a
+    lock file, so the ranks of one node started together build once."""
+    import fcntl
     os.makedirs(BUILD, exist_ok=True)
+    with open(os.path.join(BUILD, ".lock"), "w") as lk:
+        fcntl.flock(lk, fcntl.LOCK_EX)
+        try:
+            return _build_locked(verbose, force)
+        finally:
+            fcntl.flock(lk, fcntl.LOCK_UN)
+
+
+def _build_locked(verbose: bool, force: bool) -> str:
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
     headers.append(os.path.join(INCLUDE, "sc_b200.h"))
     jobs, objs = [], []
@@ -70,8 +84,10 @@ def build(verbose: bool = False, force: bool = False) -> str:
             if verbose and out:
                 print(out)
     if force or jobs or not _newer(LIB, objs):
+        tmp = f"{LIB}.tmp{os.getpid()}"  # renamed into place: a reader never sees a partial file
         _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-Xcompiler", "-fPIC", "-Xlinker",
-              "--exclude-libs,ALL", *objs, "-o", LIB, "-lpthread"])
+              "--exclude-libs,ALL", *objs, "-o", tmp, "-lpthread"])
+        os.replace(tmp, LIB)
     build_apps(force=force)
     return LIB
 

@@ -1,14 +1,19 @@
-// Instantiates the kernels of one kernel_m (SC_KM, set by the build) so the
-// six instantiation sets compile in parallel.
+// Instantiates one part of the kernels of one kernel_m: SC_KM (1..6) and
+// SC_PART (0 = wide kernels, 1 = narrow kernels) are set by the build, so the
+// instantiation sets compile in parallel.
 #include "sc_kernels.cuh"
 
 #ifndef SC_KM
 #error "SC_KM must be defined (1..6)"
 #endif
+#ifndef SC_PART
+#error "SC_PART must be defined (0 wide, 1 narrow)"
+#endif
 
 #define SC_CAT2(a, b) a##b
 #define SC_CAT(a, b) SC_CAT2(a, b)
 
+#if SC_PART == 0
 sc::WideFn SC_CAT(sc_wide_kernel_km, SC_KM)(int vec, bool batch) {
   if (batch) {
     switch (vec) {
@@ -23,7 +28,7 @@ sc::WideFn SC_CAT(sc_wide_kernel_km, SC_KM)(int vec, bool batch) {
     default: return sc::spmm_wide_kernel<SC_KM, 4, false>;
   }
 }
-
+#else
 template <int VT>
 static sc::NarrowFn narrow_of(int nb) {
   switch (nb) {
@@ -37,3 +42,4 @@ static sc::NarrowFn narrow_of(int nb) {
 sc::NarrowFn SC_CAT(sc_narrow_kernel_km, SC_KM)(int nb, int vt) {
   return vt == 1 ? narrow_of<1>(nb) : (vt == 2 ? narrow_of<2>(nb) : narrow_of<0>(nb));
 }
+#endif

@@ -19,11 +19,13 @@
 // per (panel, pattern) pair and combined them with atomicAdd
 // (example_cuda/spmm_demo_gpu_utils.h:1411-1416).
 //
-// Specialisation: the mask of each item is dispatched (binary search over
-// compile-time masks) to a body instantiated for that exact mask, so the
-// rows it feeds are compile-time register indices -- the role of the
-// reference's generated PatternWith{m}NNZByRowPanel{P} functions
-// (code_gen/spmm/spmm_format_code_generator.py:121-223).
+// Specialisation: for kernel_m <= 4 the mask of each item is dispatched
+// (binary search over compile-time masks) to a body instantiated for that
+// exact mask, so the rows it feeds are compile-time register indices -- the
+// role of the reference's generated PatternWith{m}NNZByRowPanel{P} functions
+// (code_gen/spmm/spmm_format_code_generator.py:121-223).  For kernel_m 5 and
+// 6 (31 and 63 masks) the body is specialised on the popcount, with the rows
+// read from the mask once per item.
 #pragma once
 
 #include <cstdint>
@@ -32,6 +34,11 @@
 #include <cuda_runtime.h>
 
 namespace sc {
+
+// kernel_m up to which items dispatch to a body per pattern mask.
+#ifndef SC_MASK_KM_MAX
+#define SC_MASK_KM_MAX 4
+#endif
 
 #ifndef SC_NARROW_PREFETCH
 #define SC_NARROW_PREFETCH 1
@@ -248,17 +255,96 @@ __device__ __forceinline__ void seg_wide(const uint32_t *rbuf, int len, const ch
   }
 }
 
+// acc[row of the p-th set bit of mask] += t[p], for p < P (P == popc(mask)).
+template <int KM, int P, int W>
+__device__ __forceinline__ void add_rows(int mask, const float (&t)[P][W], float (&acc)[KM][W]) {
+  int m = mask;
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    const int r = __ffs(m) - 1;
+    m &= m - 1;
+#pragma unroll
+    for (int k = p; k <= KM - P + p; ++k)
+      if (r == k) {
+#pragma unroll
+        for (int q = 0; q < W; ++q) acc[k][q] += t[p][q];
+      }
+  }
+}
+
+// Popcount-class body (kernel_m above SC_MASK_KM_MAX): specialised on the
+// pattern's popcount P, with the rows of its P set bits taken from the mask
+// at run time.  Sums go to item-local registers t[P][VEC] and are added to
+// the panel's rows once per item; the p-th set bit lies in rows
+// [p, KM-P+p], so the add is a short unrolled, predicated chain.
+template <int KM, int P, int VEC>
+__device__ __forceinline__ void seg_wide_pc(const uint32_t *rbuf, int len, const char *__restrict__ Bcol,
+                                            uint32_t ldb_bytes, bool active, int mask, float (&acc)[KM][VEC]) {
+  constexpr int S = rec_stride(P);
+  constexpr int U = P <= 2 ? SC_WIDE_U : 4;
+  float t[P][VEC];
+#pragma unroll
+  for (int p = 0; p < P; ++p)
+#pragma unroll
+    for (int q = 0; q < VEC; ++q) t[p][q] = 0.f;
+  for (int e0 = 0; e0 < len; e0 += U) {
+    float v[U][P];
+    float b[U][VEC];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      uint32_t col;
+      lds_rec<P>(rbuf + min(e0 + u, len - 1) * S, col, v[u]);
+      if (active && e0 + u < len) {
+        load_b<VEC>(reinterpret_cast<const float *>(Bcol + (uint64_t)col * ldb_bytes), b[u]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) b[u][q] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) t[p][q] = fmaf(v[u][p], b[u][q], t[p][q]);
+  }
+  add_rows<KM, P, VEC>(mask, t, acc);
+}
+
 template <int KM, int VEC, int LO, int HI>
-__device__ __forceinline__ void dispatch_wide(int mask, const uint32_t *rbuf, int len,
-                                              const char *__restrict__ Bcol, uint32_t ldb_bytes, bool active,
-                                              float (&acc)[KM][VEC]) {
+__device__ __forceinline__ void dispatch_wide_pc(int mask, const uint32_t *rbuf, int len,
+                                                 const char *__restrict__ Bcol, uint32_t ldb_bytes, bool active,
+                                                 float (&acc)[KM][VEC]) {
+  if constexpr (HI - LO == 1) {
+    seg_wide_pc<KM, LO, VEC>(rbuf, len, Bcol, ldb_bytes, active, mask, acc);
+  } else {
+    constexpr int MID = (LO + HI) / 2;
+    if (__popc(mask) < MID) dispatch_wide_pc<KM, VEC, LO, MID>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+    else dispatch_wide_pc<KM, VEC, MID, HI>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+  }
+}
+
+template <int KM, int VEC, int LO, int HI>
+__device__ __forceinline__ void dispatch_wide_mask(int mask, const uint32_t *rbuf, int len,
+                                                   const char *__restrict__ Bcol, uint32_t ldb_bytes, bool active,
+                                                   float (&acc)[KM][VEC]) {
   if constexpr (HI - LO == 1) {
     seg_wide<KM, LO, VEC>(rbuf, len, Bcol, ldb_bytes, active, acc);
   } else {
     constexpr int MID = (LO + HI) / 2;
-    if (mask < MID) dispatch_wide<KM, VEC, LO, MID>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
-    else dispatch_wide<KM, VEC, MID, HI>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+    if (mask < MID) dispatch_wide_mask<KM, VEC, LO, MID>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+    else dispatch_wide_mask<KM, VEC, MID, HI>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
   }
+}
+
+// Item dispatch: a body per mask for kernel_m <= SC_MASK_KM_MAX (2^KM - 1
+// bodies), a body per popcount above it (KM bodies: the mask-specialised
+// kernel_m = 6 kernels alone took ~20 minutes of nvcc time).
+template <int KM, int VEC>
+__device__ __forceinline__ void dispatch_wide(int mask, const uint32_t *rbuf, int len, const char *__restrict__ Bcol,
+                                              uint32_t ldb_bytes, bool active, float (&acc)[KM][VEC]) {
+  if constexpr (KM <= SC_MASK_KM_MAX) dispatch_wide_mask<KM, VEC, 1, (1 << KM)>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+  else dispatch_wide_pc<KM, VEC, 1, KM + 1>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
 }
 
 // Dynamic shared memory: max(2 record buffers per warp, the cross-warp
@@ -317,7 +403,7 @@ spmm_wide_kernel(WideArgs one, const WideArgs *__restrict__ many, const int32_t 
     cp_async_commit();
     cp_async_wait_1();
     __syncwarp();
-    dispatch_wide<KM, VEC, 1, (1 << KM)>(item.y & 0xffff, rbuf + buf * kRecBufWords, item.y >> 16, Bcol,
+    dispatch_wide<KM, VEC>(item.y & 0xffff, rbuf + buf * kRecBufWords, item.y >> 16, Bcol,
                                          one.ldb_bytes, active, acc);
     __syncwarp();
     buf ^= 1;
@@ -469,17 +555,78 @@ __device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ recs, ui
   }
 }
 
+// Popcount-class body of the narrow kernel (kernel_m above SC_MASK_KM_MAX);
+// see seg_wide_pc.
+template <int KM, int P, int NB, int VT>
+__device__ __forceinline__ void seg_narrow_pc(const uint32_t *__restrict__ recs, uint32_t off, int len,
+                                              const float *__restrict__ B, int64_t ldb, int lane, int mask,
+                                              float (&acc)[KM][NB]) {
+  constexpr int S = rec_stride(P);
+  constexpr int U = kNarrowUnroll;
+  float t[P][NB];
+#pragma unroll
+  for (int p = 0; p < P; ++p)
+#pragma unroll
+    for (int q = 0; q < NB; ++q) t[p][q] = 0.f;
+  for (int e0 = 0; e0 < len; e0 += 32 * U) {
+    int col[U];
+    float v[U][P];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = e0 + u * 32 + lane;
+      if (e < len) {
+        load_rec_any<P, VT>(recs, off + (uint32_t)(e * S), col[u], v[u]);
+      } else {
+        col[u] = 0;
+#pragma unroll
+        for (int p = 0; p < P; ++p) v[u][p] = 0.f;
+      }
+    }
+    float b[U][NB];
+#pragma unroll
+    for (int u = 0; u < U; ++u) load_vec<NB>(B + (int64_t)col[u] * ldb, b[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int q = 0; q < NB; ++q) t[p][q] = fmaf(v[u][p], b[u][q], t[p][q]);
+  }
+  add_rows<KM, P, NB>(mask, t, acc);
+}
+
 template <int KM, int NB, int VT, int LO, int HI>
-__device__ __forceinline__ void dispatch_narrow(int mask, const uint32_t *__restrict__ recs, uint32_t off, int len,
-                                                const float *__restrict__ B, int64_t ldb, int lane,
-                                                float (&acc)[KM][NB]) {
+__device__ __forceinline__ void dispatch_narrow_mask(int mask, const uint32_t *__restrict__ recs, uint32_t off,
+                                                     int len, const float *__restrict__ B, int64_t ldb, int lane,
+                                                     float (&acc)[KM][NB]) {
   if constexpr (HI - LO == 1) {
     seg_narrow<KM, LO, NB, VT>(recs, off, len, B, ldb, lane, acc);
   } else {
     constexpr int MID = (LO + HI) / 2;
-    if (mask < MID) dispatch_narrow<KM, NB, VT, LO, MID>(mask, recs, off, len, B, ldb, lane, acc);
-    else dispatch_narrow<KM, NB, VT, MID, HI>(mask, recs, off, len, B, ldb, lane, acc);
+    if (mask < MID) dispatch_narrow_mask<KM, NB, VT, LO, MID>(mask, recs, off, len, B, ldb, lane, acc);
+    else dispatch_narrow_mask<KM, NB, VT, MID, HI>(mask, recs, off, len, B, ldb, lane, acc);
   }
+}
+
+template <int KM, int NB, int VT, int LO, int HI>
+__device__ __forceinline__ void dispatch_narrow_pc(int mask, const uint32_t *__restrict__ recs, uint32_t off,
+                                                   int len, const float *__restrict__ B, int64_t ldb, int lane,
+                                                   float (&acc)[KM][NB]) {
+  if constexpr (HI - LO == 1) {
+    seg_narrow_pc<KM, LO, NB, VT>(recs, off, len, B, ldb, lane, mask, acc);
+  } else {
+    constexpr int MID = (LO + HI) / 2;
+    if (__popc(mask) < MID) dispatch_narrow_pc<KM, NB, VT, LO, MID>(mask, recs, off, len, B, ldb, lane, acc);
+    else dispatch_narrow_pc<KM, NB, VT, MID, HI>(mask, recs, off, len, B, ldb, lane, acc);
+  }
+}
+
+template <int KM, int NB, int VT>
+__device__ __forceinline__ void dispatch_narrow(int mask, const uint32_t *__restrict__ recs, uint32_t off, int len,
+                                                const float *__restrict__ B, int64_t ldb, int lane,
+                                                float (&acc)[KM][NB]) {
+  if constexpr (KM <= SC_MASK_KM_MAX) dispatch_narrow_mask<KM, NB, VT, 1, (1 << KM)>(mask, recs, off, len, B, ldb, lane, acc);
+  else dispatch_narrow_pc<KM, NB, VT, 1, KM + 1>(mask, recs, off, len, B, ldb, lane, acc);
 }
 
 __host__ __device__ constexpr int pow2_ceil(int x) {
@@ -567,7 +714,7 @@ spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ i
     const int2 mine = lane < cnt ? __ldg(items + it0 + warp + (base + lane) * nw) : make_int2(0, 0);
     for (int j = 0; j < cnt; ++j) {
       const int2 item = make_int2(__shfl_sync(0xffffffffu, mine.x, j), __shfl_sync(0xffffffffu, mine.y, j));
-      dispatch_narrow<KM, NB, VT, 1, (1 << KM)>(item.y & 0xffff, recs, (uint32_t)item.x, item.y >> 16, B, ldb,
+      dispatch_narrow<KM, NB, VT>(item.y & 0xffff, recs, (uint32_t)item.x, item.y >> 16, B, ldb,
                                                 lane, acc);
     }
   }
