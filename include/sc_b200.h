@@ -37,6 +37,8 @@ extern "C" {
 #define SC_ERR_CUDA 4        /* a CUDA runtime call failed */
 #define SC_ERR_UNSUPPORTED 5 /* valid input outside what this build handles */
 #define SC_ERR_NOMEM 6       /* host allocation failed */
+#define SC_ERR_DEVICE 7      /* a bounded wait inside a kernel expired: that
+                                product's C is incomplete (see sc_plan_status) */
 
 typedef struct sc_csr sc_csr;   /* CSR matrix, int32 indices, float64 values */
 typedef struct sc_cf sc_cf;     /* pattern-compressed ("CF") matrix, one block per pattern */
@@ -147,6 +149,11 @@ int sc_plan_create_panels(const sc_cf *cf, int32_t n_cols_b, int32_t device,
 #define SC_PLAN_DENSE_BF16 4u
 #define SC_PLAN_VALUES_F16 8u
 #define SC_PLAN_VALUES_BF16 16u
+/* Test hook for the error path, not for production: in a dense-tile plan's
+ * kernel the producer issues no copies, so the MMA issuer's bounded wait
+ * expires with nothing in flight; every product of the plan then leaves C
+ * unwritten and sets status 2/3 (sc_plan_status, SC_ERR_DEVICE). */
+#define SC_PLAN_TEST_STARVE (1u << 30)
 int sc_plan_create_ex(const sc_cf *cf, int32_t n_cols_b, int32_t device, int64_t panel_begin,
                       int64_t panel_end, uint32_t flags, sc_plan **out);
 
@@ -208,6 +215,16 @@ int sc_spmv(sc_plan *p, const float *dx, float *dy, int32_t accumulate, void *st
  * on the device and copied back in row chunks that overlap the remaining
  * kernels. */
 int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream);
+/* Device-side error status of a plan's kernels since the last call: waits
+ * for all work on the plan's device (cudaDeviceSynchronize), copies the
+ * plan's status word to *status and clears it.  0 = no error; 1, 2, 3 = a
+ * bounded mbarrier wait of the dense-tile kernel expired (producer, MMA
+ * issuer, epilogue) and that CTA skipped its C stores.  Only dense-tile plans
+ * (sc_plan_info.kernel == 3) have waits inside the kernel; other plans
+ * always report 0.  sc_spmm_host checks it itself and returns SC_ERR_DEVICE.
+ * The reference checks no kernel status (example_cuda/spmm_demo_gpu_utils.h:16-23
+ * checks launch errors only). */
+int sc_plan_status(sc_plan *p, int32_t *status);
 void sc_plan_free(sc_plan *p);
 
 /* ------------------------------------------------------ allocation-free -- */
@@ -223,10 +240,17 @@ void sc_plan_free(sc_plan *p);
  * blocks plus B, at 8 bytes per element -- are rejected with SC_ERR_ARG.
  * n must be a multiple of 128; C rows 16-byte aligned.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress), so make
- * that first call before any stream capture.  Calls share the array: calls
- * that overlap on the GPU (different streams at once) race. */
+ * that first call before any stream capture; the address is kept for the
+ * life of the process, so a cudaDeviceReset while the library is loaded is
+ * not supported.  Calls share the array: calls that overlap on the GPU
+ * (different streams at once) race. */
 int sc_spmm_dense_noalloc(const float *dA, int64_t lda, int64_t m, int64_t k, const float *dB, int64_t ldb,
                           int64_t n, float *dC, int64_t ldc, int32_t accumulate, void *stream);
+/* Status word of sc_spmm_dense_noalloc on the current device (same codes as
+ * sc_plan_status): waits for the device, copies the word (it lives in the
+ * shared scratch array, so it reports the last call that ran) and clears it.
+ * Allocates nothing. */
+int sc_noalloc_status(int32_t *status);
 
 /* ------------------------------------------------------------- batches ---- */
 
@@ -246,6 +270,8 @@ int sc_batch_bind(sc_batch *b, const float *const *dB, const int64_t *ldb, float
                   const int64_t *ldc);
 /* C_i = A_i*B_i (or +=) for all plans of the batch, one kernel launch. */
 int sc_batch_spmm(sc_batch *b, int32_t accumulate, void *stream);
+/* sc_plan_status for the dense-tile launch of a batch (its own status word). */
+int sc_batch_status(sc_batch *b, int32_t *status);
 void sc_batch_free(sc_batch *b);
 
 /* ---------------------------------------------------------------- graphs -- */

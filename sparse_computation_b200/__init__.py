@@ -40,6 +40,7 @@ SC_ERR_FORMAT = 3
 SC_ERR_CUDA = 4
 SC_ERR_UNSUPPORTED = 5
 SC_ERR_NOMEM = 6
+SC_ERR_DEVICE = 7
 
 # sc_plan_create_ex flags
 SC_PLAN_DENSE_OFF = 1
@@ -47,6 +48,7 @@ SC_PLAN_DENSE_ON = 2
 SC_PLAN_DENSE_BF16 = 4
 SC_PLAN_VALUES_F16 = 8
 SC_PLAN_VALUES_BF16 = 16
+SC_PLAN_TEST_STARVE = 1 << 30  # test hook: dense-tile waits expire (error path tests)
 
 # Every symbol include/sc_b200.h declares (checked by the CPU tests).
 EXPORTED_SYMBOLS = (
@@ -58,7 +60,7 @@ EXPORTED_SYMBOLS = (
     "sc_plan_create", "sc_plan_create_panels", "sc_plan_create_ex", "sc_plan_get_info", "sc_spmm", "sc_spmv",
     "sc_spmm_host", "sc_plan_free", "sc_spmm_peers", "sc_wait_flags",
     "sc_batch_create", "sc_batch_bind", "sc_batch_spmm", "sc_batch_free",
-    "sc_spmm_dense_noalloc",
+    "sc_spmm_dense_noalloc", "sc_noalloc_status", "sc_plan_status", "sc_batch_status",
     "sc_graph_capture_plan", "sc_graph_capture_batch", "sc_graph_launch", "sc_graph_free",
 )
 
@@ -139,6 +141,9 @@ def lib() -> ctypes.CDLL:
         "sc_graph_launch": ([vp, vp], ctypes.c_int),
         "sc_graph_free": ([vp], None),
         "sc_spmm_dense_noalloc": ([vp, i64, i64, i64, vp, i64, i64, vp, i64, i32, vp], ctypes.c_int),
+        "sc_noalloc_status": ([P(i32)], ctypes.c_int),
+        "sc_plan_status": ([vp, P(i32)], ctypes.c_int),
+        "sc_batch_status": ([vp, P(i32)], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -352,6 +357,14 @@ def wait_flags(flags_ptr: int, n: int, epoch: int, status_ptr: int, stream) -> N
                                ctypes.c_void_p(stream.cuda_stream)))
 
 
+def noalloc_status() -> int:
+    """sc_noalloc_status: error status of the last sc_spmm_dense_noalloc on
+    the current device (waits for the device, then clears it)."""
+    v = ctypes.c_int32()
+    _check(lib().sc_noalloc_status(ctypes.byref(v)))
+    return v.value
+
+
 def _torch():
     import torch
     return torch
@@ -462,6 +475,20 @@ class SpMMPlan:
         _check(lib().sc_spmm_host(self._h, ctypes.c_void_p(B.ctypes.data), ctypes.c_void_p(C.ctypes.data), s))
         return C
 
+    def status(self) -> int:
+        """Device-side error status of this plan's kernels since the last
+        call (waits for the device, then clears it): 0 = none; 1-3 = a
+        bounded wait of the dense-tile kernel expired and C is incomplete."""
+        v = ctypes.c_int32()
+        _check(lib().sc_plan_status(self._h, ctypes.byref(v)))
+        return v.value
+
+    def check(self) -> None:
+        """Raises ScError(SC_ERR_DEVICE) when status() is non-zero."""
+        v = self.status()
+        if v:
+            raise ScError(SC_ERR_DEVICE, f"a bounded device wait expired (status {v}); C is incomplete")
+
     def __del__(self):
         if getattr(self, "_h", None) and self._h.value and _lib is not None:
             _lib.sc_plan_free(self._h)
@@ -509,6 +536,12 @@ class SpMMBatch:
         h = ctypes.c_void_p()
         _check(lib().sc_graph_capture_batch(self._h, 1 if accumulate else 0, repeat, ctypes.byref(h)))
         return Graph(h.value, self.plans[0].device, keep=(self,))
+
+    def status(self) -> int:
+        """sc_batch_status: the dense-tile launch's error status (see SpMMPlan.status)."""
+        v = ctypes.c_int32()
+        _check(lib().sc_batch_status(self._h, ctypes.byref(v)))
+        return v.value
 
     def __del__(self):
         if getattr(self, "_h", None) and self._h.value and _lib is not None:

@@ -11,6 +11,7 @@
 //              32w..32w+31 = C rows), then row-contiguous stores of C.
 // Every wait on an mbarrier is bounded; on expiry the CTA records an error in
 // *status, stops issuing work, and still releases its tensor memory.
+#include <atomic>
 #include <cstring>
 
 #include <cooperative_groups.h>
@@ -180,7 +181,7 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (threadIdx.x == 0 && nk > 0) {
+  if (threadIdx.x == 0 && nk > 0 && !m.starve) {
     // producer
     constexpr int OP = BF16 ? kTileBytes : 2 * kTileBytes;  // bytes of one operand's images
     for (int i = 0; i < nk; ++i) {
@@ -405,14 +406,16 @@ int sc_dense_gemm(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mat
   const size_t smem = (size_t)kStages * kStageBytes + 1024;
   auto fn = mats ? (bf16 ? dense_gemm_kernel<true, true> : dense_gemm_kernel<true, false>)
                  : (bf16 ? dense_gemm_kernel<false, true> : dense_gemm_kernel<false, false>);
-  static unsigned attr_done[4] = {0, 0, 0, 0};  // one bit per device ordinal (< 32)
+  // one bit per device ordinal (< 32); concurrent callers may both set the
+  // attribute, which is harmless, and the bit update is atomic
+  static std::atomic<unsigned> attr_done[4];
   int dev = 0;
   cudaGetDevice(&dev);
-  unsigned &bits = attr_done[(mats ? 1 : 0) + (bf16 ? 2 : 0)];
-  if (dev >= 32 || !(bits & (1u << dev))) {
+  std::atomic<unsigned> &bits = attr_done[(mats ? 1 : 0) + (bf16 ? 2 : 0)];
+  if (dev >= 32 || !(bits.load() & (1u << dev))) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;
-    if (dev < 32) bits |= 1u << dev;
+    if (dev < 32) bits.fetch_or(1u << dev);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(ntasks * split), 1, 1);

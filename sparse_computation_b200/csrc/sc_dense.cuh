@@ -90,6 +90,8 @@ struct DenseMat {
   int k_chunks;             // ceil(K / 32), or ceil(K / 64) in bf16 mode
   int n_tiles;              // N / 128
   int bf16;                 // 1: bf16 tiles (one image per operand)
+  int starve = 0;           // test hook: the producer issues no copies, so the
+                            // MMA issuer's bounded wait expires (status 2, then 3)
 };
 
 }  // namespace dense

@@ -30,7 +30,9 @@ std::mutex g_scratch_mu;
 
 // Device address of the scratch array on the current device.  In host code
 // the array's name is only a host-side stand-in, so its device address must
-// be asked for once per device, with that device current.
+// be asked for once per device, with that device current.  The address is
+// kept for the life of the process: a cudaDeviceReset (which discards the
+// module and its array) is not supported while this library is loaded.
 int scratch_for_current_device(uint8_t **out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
@@ -86,6 +88,7 @@ __global__ void noalloc_init(int rbs, int kcs, int nts, int32_t *rb_ptr, int32_t
 }
 
 size_t align1k(size_t x) { return (x + 1023) & ~(size_t)1023; }
+constexpr size_t kStatusBytes = 1024;
 
 }  // namespace
 
@@ -108,13 +111,15 @@ extern "C" int sc_spmm_dense_noalloc(const float *dA, int64_t lda, int64_t m, in
     return SC_ERR_ARG;
   }
   const int64_t rbs = (m + kBM - 1) / kBM, kcs = std::max<int64_t>(1, (k + kBK - 1) / kBK), nts = n / kBN;
-  // scratch layout: A tiles | B tiles | rb_ptr | rb_chunk | tasks | status
-  const size_t o_b = align1k((size_t)rbs * kcs * 2 * kTileBytes);
+  // scratch layout: status (first 1 KiB, at a fixed place so that
+  // sc_noalloc_status finds it) | A tiles | B tiles | rb_ptr | rb_chunk | tasks
+  const size_t o_a = kStatusBytes;
+  const size_t o_b = o_a + align1k((size_t)rbs * kcs * 2 * kTileBytes);
   const size_t o_ptr = o_b + align1k((size_t)nts * kcs * 2 * kTileBytes);
   const size_t o_chunk = o_ptr + align1k((size_t)(rbs + 1) * 4);
   const size_t o_tasks = o_chunk + align1k((size_t)rbs * kcs * 4);
-  const size_t o_status = o_tasks + align1k((size_t)rbs * nts * sizeof(int4));
-  const size_t need = o_status + 1024;
+  const size_t need = o_tasks + align1k((size_t)rbs * nts * sizeof(int4));
+  const size_t o_status = 0;
   if (need > kNoAllocScratchBytes) {
     sc_set_error("sc_spmm_dense_noalloc: needs " + std::to_string(need) + " bytes of scratch, more than the " +
                  std::to_string(kNoAllocScratchBytes) +
@@ -130,7 +135,7 @@ extern "C" int sc_spmm_dense_noalloc(const float *dA, int64_t lda, int64_t m, in
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DenseMat mat;
-  mat.a_tiles = base;
+  mat.a_tiles = base + o_a;
   mat.rb_ptr = reinterpret_cast<const int32_t *>(base + o_ptr);
   mat.rb_chunk = reinterpret_cast<const int32_t *>(base + o_chunk);
   mat.b_tiles = base + o_b;
@@ -148,7 +153,7 @@ extern "C" int sc_spmm_dense_noalloc(const float *dA, int64_t lda, int64_t m, in
   noalloc_init<<<(unsigned)((cells + 255) / 256), 256, 0, s>>>(
       (int)rbs, (int)kcs, (int)nts, const_cast<int32_t *>(mat.rb_ptr), const_cast<int32_t *>(mat.rb_chunk),
       reinterpret_cast<int4 *>(base + o_tasks), reinterpret_cast<int *>(base + o_status));
-  noalloc_split_a<<<dim3((unsigned)kcs, (unsigned)rbs), 256, 0, s>>>(dA, lda, m, k, (int)kcs, base);
+  noalloc_split_a<<<dim3((unsigned)kcs, (unsigned)rbs), 256, 0, s>>>(dA, lda, m, k, (int)kcs, base + o_a);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) e = (cudaError_t)sc_dense_split_b(mat, nullptr, 1, (int)(nts * kcs), false, s);
   // split K over a cluster when the tiles are too few to fill the GPU
@@ -161,5 +166,26 @@ extern "C" int sc_spmm_dense_noalloc(const float *dA, int64_t lda, int64_t m, in
     sc_set_error(std::string("sc_spmm_dense_noalloc: launch: ") + cudaGetErrorString(e));
     return SC_ERR_CUDA;
   }
+  return SC_OK;
+}
+
+extern "C" int sc_noalloc_status(int32_t *status) {
+  if (!status) {
+    sc_set_error("sc_noalloc_status: null argument");
+    return SC_ERR_ARG;
+  }
+  *status = 0;
+  uint8_t *base = nullptr;
+  int err = scratch_for_current_device(&base);
+  cudaError_t e = (cudaError_t)err;
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  int v = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&v, base, 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && v) e = cudaMemset(base, 0, 4);
+  if (e != cudaSuccess) {
+    sc_set_error(std::string("sc_noalloc_status: ") + cudaGetErrorString(e));
+    return SC_ERR_CUDA;
+  }
+  *status = v;
   return SC_OK;
 }

@@ -215,6 +215,7 @@ sc::dense::DenseMat dense_mat(const sc_plan *p, const float *B, int64_t ldb, flo
   m.k_chunks = (int)((p->cols + bk - 1) / bk);
   m.n_tiles = (int)(p->n / sc::dense::kBN);
   m.bf16 = p->dense_bf16 ? 1 : 0;
+  m.starve = (p->flags & SC_PLAN_TEST_STARVE) ? 1 : 0;
   return m;
 }
 
@@ -712,6 +713,25 @@ void launch_khalf(sc_plan *p, int h, float *C, float *host_c, cudaStream_t strea
   cuda_check(cudaGetLastError(), "kernel launch");
 }
 
+// Waits for the current device, reads a device status word and clears it.
+int take_status(int *dstatus) {
+  cuda_check(cudaDeviceSynchronize(), "device synchronize");
+  int v = 0;
+  cuda_check(cudaMemcpy(&v, dstatus, 4, cudaMemcpyDeviceToHost), "read status");
+  if (v) cuda_check(cudaMemset(dstatus, 0, 4), "clear status");
+  return v;
+}
+
+// After a synchronous product: a dense-tile CTA whose bounded wait expired
+// skipped its C stores, so the call must not report success.
+void check_plan_status(sc_plan *p) {
+  if (!p->status) return;
+  const int v = take_status(p->status);
+  if (v)
+    throw sc_error(SC_ERR_DEVICE, "dense-tile kernel: a bounded device wait expired (status " + std::to_string(v) +
+                                      "); C is incomplete");
+}
+
 }  // namespace
 
 #define SC_API_BEGIN try {
@@ -756,7 +776,7 @@ int sc_plan_create_ex(const sc_cf *cf, int32_t n_cols_b, int32_t device, int64_t
   require(panel_begin == -1 ? panel_end == -1 : (panel_begin >= 0 && panel_end >= panel_begin), SC_ERR_ARG,
           "bad panel range (both -1 for the whole matrix)");
   require((flags & ~(uint32_t)(SC_PLAN_DENSE_OFF | SC_PLAN_DENSE_ON | SC_PLAN_DENSE_BF16 | SC_PLAN_VALUES_F16 |
-                                SC_PLAN_VALUES_BF16)) == 0,
+                                SC_PLAN_VALUES_BF16 | SC_PLAN_TEST_STARVE)) == 0,
           SC_ERR_ARG, "unknown plan flag");
   require(!((flags & SC_PLAN_VALUES_F16) && (flags & SC_PLAN_VALUES_BF16)), SC_ERR_ARG,
           "SC_PLAN_VALUES_F16 and SC_PLAN_VALUES_BF16 exclude each other");
@@ -912,7 +932,7 @@ int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream) {
     cuda_check(cudaStreamWaitEvent(s, ev[4], 0), "wait event");
     launch_khalf(p, 1, p->stage_c, dC_host, s);
     cuda_check(cudaStreamSynchronize(s), "stream synchronize");
-    return SC_OK;
+    return SC_OK;  // wide plan: no device-side waits
   }
   if (bb >= (1u << 20)) {
     // two concurrent copies (this stream + the side stream): one DMA stream
@@ -954,6 +974,17 @@ int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream) {
     cuda_check(cudaStreamSynchronize(p->side), "stream synchronize");
     cuda_check(cudaStreamSynchronize(s), "stream synchronize");
   }
+  check_plan_status(p);
+  SC_API_END
+}
+
+int sc_plan_status(sc_plan *p, int32_t *status) {
+  SC_API_BEGIN
+  require(p != nullptr && status != nullptr, SC_ERR_ARG, "null argument");
+  *status = 0;
+  if (!p->status) return SC_OK;
+  DeviceGuard dg(p->device);
+  *status = take_status(p->status);
   SC_API_END
 }
 
@@ -1119,6 +1150,16 @@ int sc_batch_bind(sc_batch *b, const float *const *dB, const int64_t *ldb, float
     cuda_check(cudaMemcpy(b->dmats, dm.data(), dm.size() * sizeof(sc::dense::DenseMat), cudaMemcpyHostToDevice),
                "upload batch operands");
   b->bound = true;
+  SC_API_END
+}
+
+int sc_batch_status(sc_batch *b, int32_t *status) {
+  SC_API_BEGIN
+  require(b != nullptr && status != nullptr, SC_ERR_ARG, "null argument");
+  *status = 0;
+  if (!b->status) return SC_OK;
+  DeviceGuard dg(b->device);
+  *status = take_status(b->status);
   SC_API_END
 }
 

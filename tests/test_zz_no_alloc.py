@@ -64,3 +64,34 @@ def test_noalloc_rejects_oversized_inputs(cuda):
     B2 = torch.zeros((4096, 100), device=cuda)
     C2 = torch.zeros((4096, 100), device=cuda)
     assert _call_noalloc(A[:128, :64], B2[:64], C2[:128]) == sc.SC_ERR_UNSUPPORTED
+
+
+def test_noalloc_ragged_strided_and_accumulate(cuda):
+    """Shapes that are not multiples of the tiles (m % 128, k % 32), a leading
+    dimension wider than k, then C += A*B on the same C: each call checked
+    against the CPU oracle at the fp32 bound, and the status word stays 0."""
+    import torch
+    rng = np.random.default_rng(11)
+    m, k, lda, n = 200, 100, 104, 128
+    Ad = np.where(rng.random((m, k)) < 0.3, rng.normal(0, 0.05, (m, k)), 0).astype(np.float32)
+    a = wl.csr_from_dense(Ad)
+    _, _, ip, ix, dx = a
+    Apad = np.full((m, lda), np.nan, np.float32)  # the columns past k must never be read
+    Apad[:, :k] = Ad
+    A = torch.from_numpy(Apad).to(cuda)[:, :k]
+    assert A.stride(0) == lda
+    B_np = wl.dense_b(k, n, 12)
+    B = torch.from_numpy(B_np).to(cuda)
+    C = torch.full((m, n), float("nan"), device=cuda)
+    assert _call_noalloc(A, B, C, 0) == sc.SC_OK, sc.lib().sc_last_error_string()
+    first = C.cpu().numpy()
+    assert sc.noalloc_status() == 0
+    ref = cpu.spmm_csr_float(ip, ix, dx, B_np)
+    scale = cpu.spmm_csr_abs(ip, ix, dx, B_np)
+    assert np.all(np.abs(first.astype(np.float64) - ref) <= RTOL * scale)
+    assert _call_noalloc(A, B, C, 1) == sc.SC_OK, sc.lib().sc_last_error_string()
+    second = C.cpu().numpy()
+    assert sc.noalloc_status() == 0
+    ref2 = cpu.spmm_csr_float(ip, ix, dx, B_np, first.copy())
+    scale2 = scale + np.abs(first.astype(np.float64))
+    assert np.all(np.abs(second.astype(np.float64) - ref2) <= RTOL * scale2)
