@@ -11,7 +11,7 @@
 // rows the 16-byte chunk c of row r sits at chunk c ^ (r & 7).  A tiles are
 // written in this image on the host at plan time; B tiles by a small kernel
 // per call, so every stage is loaded with plain bulk copies (cp.async.bulk,
-// no tensor map, no multicast).
+// no tensor map; each copy lands in its own CTA only).
 //
 // Work: a task is (matrix, 128-row block, 128-column tile); a task's K-chunks
 // are split over a thread-block cluster of S CTAs (S in {1, 2, 4}) whose

@@ -177,11 +177,24 @@ struct WideArgs {
 #ifndef SC_B_NOALLOC
 #define SC_B_NOALLOC 0
 #endif
+// Entries whose B rows are loaded together (P <= 2), and the launch-bound
+// CTA count (256-thread units: 4 -> at most 64 registers a thread).  Measured
+// on config 5 (B200): U 8 / 3 CTAs 291 us, U 4 / 4 CTAs 251 us; more
+// resident warps (5, 6, 8) were slower (292-420 us): the B rows they share
+// through L1 are evicted sooner.  The batched kernel (many small matrices,
+// one launch) keeps U 8 / 3 CTAs: config 3 measured 24.1 us there against
+// 27.0 us with the single-matrix setting.
 #ifndef SC_WIDE_U
-#define SC_WIDE_U 8
+#define SC_WIDE_U 4
 #endif
 #ifndef SC_WIDE_MINB
-#define SC_WIDE_MINB 3
+#define SC_WIDE_MINB 4
+#endif
+#ifndef SC_WIDE_BATCH_U
+#define SC_WIDE_BATCH_U 8
+#endif
+#ifndef SC_WIDE_BATCH_MINB
+#define SC_WIDE_BATCH_MINB 3
 #endif
 constexpr int kRecBufWords = kItemEntries * 8;  // one item of the widest stride
 
@@ -225,12 +238,12 @@ __device__ __forceinline__ void lds_rec(const uint32_t *r, uint32_t &col, float 
   }
 }
 
-template <int KM, int MASK, int VEC>
+template <int KM, int MASK, int VEC, int UW>
 __device__ __forceinline__ void seg_wide(const uint32_t *rbuf, int len, const char *__restrict__ Bcol,
                                          uint32_t ldb_bytes, bool active, float (&acc)[KM][VEC]) {
   constexpr int P = popc_c(MASK);
   constexpr int S = rec_stride(P);
-  constexpr int U = P <= 2 ? SC_WIDE_U : 4;
+  constexpr int U = P <= 2 ? UW : 4;
   for (int e0 = 0; e0 < len; e0 += U) {
     float v[U][P];
     float b[U][VEC];
@@ -277,11 +290,11 @@ __device__ __forceinline__ void add_rows(int mask, const float (&t)[P][W], float
 // at run time.  Sums go to item-local registers t[P][VEC] and are added to
 // the panel's rows once per item; the p-th set bit lies in rows
 // [p, KM-P+p], so the add is a short unrolled, predicated chain.
-template <int KM, int P, int VEC>
+template <int KM, int P, int VEC, int UW>
 __device__ __forceinline__ void seg_wide_pc(const uint32_t *rbuf, int len, const char *__restrict__ Bcol,
                                             uint32_t ldb_bytes, bool active, int mask, float (&acc)[KM][VEC]) {
   constexpr int S = rec_stride(P);
-  constexpr int U = P <= 2 ? SC_WIDE_U : 4;
+  constexpr int U = P <= 2 ? UW : 4;
   float t[P][VEC];
 #pragma unroll
   for (int p = 0; p < P; ++p)
@@ -311,40 +324,40 @@ __device__ __forceinline__ void seg_wide_pc(const uint32_t *rbuf, int len, const
   add_rows<KM, P, VEC>(mask, t, acc);
 }
 
-template <int KM, int VEC, int LO, int HI>
+template <int KM, int VEC, int UW, int LO, int HI>
 __device__ __forceinline__ void dispatch_wide_pc(int mask, const uint32_t *rbuf, int len,
                                                  const char *__restrict__ Bcol, uint32_t ldb_bytes, bool active,
                                                  float (&acc)[KM][VEC]) {
   if constexpr (HI - LO == 1) {
-    seg_wide_pc<KM, LO, VEC>(rbuf, len, Bcol, ldb_bytes, active, mask, acc);
+    seg_wide_pc<KM, LO, VEC, UW>(rbuf, len, Bcol, ldb_bytes, active, mask, acc);
   } else {
     constexpr int MID = (LO + HI) / 2;
-    if (__popc(mask) < MID) dispatch_wide_pc<KM, VEC, LO, MID>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
-    else dispatch_wide_pc<KM, VEC, MID, HI>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+    if (__popc(mask) < MID) dispatch_wide_pc<KM, VEC, UW, LO, MID>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+    else dispatch_wide_pc<KM, VEC, UW, MID, HI>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
   }
 }
 
-template <int KM, int VEC, int LO, int HI>
+template <int KM, int VEC, int UW, int LO, int HI>
 __device__ __forceinline__ void dispatch_wide_mask(int mask, const uint32_t *rbuf, int len,
                                                    const char *__restrict__ Bcol, uint32_t ldb_bytes, bool active,
                                                    float (&acc)[KM][VEC]) {
   if constexpr (HI - LO == 1) {
-    seg_wide<KM, LO, VEC>(rbuf, len, Bcol, ldb_bytes, active, acc);
+    seg_wide<KM, LO, VEC, UW>(rbuf, len, Bcol, ldb_bytes, active, acc);
   } else {
     constexpr int MID = (LO + HI) / 2;
-    if (mask < MID) dispatch_wide_mask<KM, VEC, LO, MID>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
-    else dispatch_wide_mask<KM, VEC, MID, HI>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+    if (mask < MID) dispatch_wide_mask<KM, VEC, UW, LO, MID>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+    else dispatch_wide_mask<KM, VEC, UW, MID, HI>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
   }
 }
 
 // Item dispatch: a body per mask for kernel_m <= SC_MASK_KM_MAX (2^KM - 1
 // bodies), a body per popcount above it (KM bodies: the mask-specialised
 // kernel_m = 6 kernels alone took ~20 minutes of nvcc time).
-template <int KM, int VEC>
+template <int KM, int VEC, int UW>
 __device__ __forceinline__ void dispatch_wide(int mask, const uint32_t *rbuf, int len, const char *__restrict__ Bcol,
                                               uint32_t ldb_bytes, bool active, float (&acc)[KM][VEC]) {
-  if constexpr (KM <= SC_MASK_KM_MAX) dispatch_wide_mask<KM, VEC, 1, (1 << KM)>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
-  else dispatch_wide_pc<KM, VEC, 1, KM + 1>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+  if constexpr (KM <= SC_MASK_KM_MAX) dispatch_wide_mask<KM, VEC, UW, 1, (1 << KM)>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
+  else dispatch_wide_pc<KM, VEC, UW, 1, KM + 1>(mask, rbuf, len, Bcol, ldb_bytes, active, acc);
 }
 
 // Dynamic shared memory: max(2 record buffers per warp, the cross-warp
@@ -359,7 +372,7 @@ __host__ __device__ constexpr size_t wide_smem_bytes(int warps, int km, int vec)
 // BATCH == true : CTA b computes panel order2[b].y of matrix many[order2[b].x]
 //                 (a whole set of matrices -- e.g. a layer stack -- in one launch).
 template <int KM, int VEC, bool BATCH>
-__global__ void __launch_bounds__(256, SC_WIDE_MINB)
+__global__ void __launch_bounds__(256, BATCH ? SC_WIDE_BATCH_MINB : SC_WIDE_MINB)
 spmm_wide_kernel(WideArgs one, const WideArgs *__restrict__ many, const int32_t *__restrict__ order,
                  int accumulate) {
   extern __shared__ __align__(16) uint32_t smem[];
@@ -403,7 +416,7 @@ spmm_wide_kernel(WideArgs one, const WideArgs *__restrict__ many, const int32_t 
     cp_async_commit();
     cp_async_wait_1();
     __syncwarp();
-    dispatch_wide<KM, VEC>(item.y & 0xffff, rbuf + buf * kRecBufWords, item.y >> 16, Bcol,
+    dispatch_wide<KM, VEC, BATCH ? SC_WIDE_BATCH_U : SC_WIDE_U>(item.y & 0xffff, rbuf + buf * kRecBufWords, item.y >> 16, Bcol,
                                          one.ldb_bytes, active, acc);
     __syncwarp();
     buf ^= 1;

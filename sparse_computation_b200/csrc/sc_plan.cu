@@ -569,6 +569,8 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   if (plan->kernel == 2 && plan->panels > 0)
     plan->warps = wave_model_warps(km, plan->vec, false, plan->panels * slices,
                                    (double)plan->items / (double)plan->panels, plan->warps);
+  if (const char *e = getenv("SC_WIDE_WARPS"))  // tuning experiments: fixed warps per panel
+    if (plan->kernel == 2 && atoi(e) >= 1 && atoi(e) <= 8) plan->warps = atoi(e);
   auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
   const size_t b_recs = align(recs.size() * 4);
   const size_t b_items = align(std::max<size_t>(1, items.size()) * sizeof(int2));
