@@ -22,6 +22,7 @@ timed events.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -323,6 +324,81 @@ def cusparse_baseline(mats, dev, flush, args):
                 "how": "torch.sparse_csr_tensor @ dense (cusparseSpMM, CSR int32, row-major)"}
     except Exception as ex:  # reported baseline only
         return {"unavailable": str(ex)[:200]}
+
+
+def reference_gpu_baseline(mats, flush, args):
+    """The reference's own GPU kernel for this product, compiled from its
+    headers for sm_100a into oracle/_ref (a reported baseline, never the
+    product path): SpMMFullRowPanelGeneralKernel4With2BlockCacheLess for N > 4
+    (generated for coarsening (4, 2)), SpmvComplexPatternDecomposeByRowSeperated
+    for N = 1 (coarsening (4, 1)).  Run as the reference's benchmark runs it --
+    one .cfmtx read by its loader, C zeroed outside the timed region, one launch
+    per step timed with CUDA events -- with the L2 flushed before each step like
+    our kernel."""
+    import tempfile
+
+    import torch
+
+    import sparse_computation_b200 as sc
+    from oracle import cpu
+    if len(mats) != 1:
+        return {"unavailable": "single-matrix workloads only"}
+    (m, n, ip, ix, dx), B = mats[0]
+    N = B.shape[1]
+    spmv = N == 1
+    so = "libref_gpu_spmv.so" if spmv else "libref_gpu_spmm.so"
+    if N not in (1, 128) and not (N > 4 and N % 32 == 0):
+        return {"unavailable": f"the reference's generated kernels cover N = 1 and N > 4 (multiple of 32), not {N}"}
+    if not cpu.ref_available(so):
+        return {"unavailable": f"oracle/_ref/{so} not built (needs the reference sources at build time)"}
+    L = cpu.ref_lib(so)
+    pre = "ref_gpu_spmv_" if spmv else "ref_gpu_spmm_"
+    fn = lambda name: getattr(L, pre + name)  # noqa: E731
+    kn = 1 if spmv else 2
+    cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(m, n, ip, ix, dx), 4, kn)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, f"matrix-4-{kn}.cfmtx")
+        cf.write(path)
+        Bc = np.ascontiguousarray(B[:, 0] if spmv else B, np.float32)
+        h = fn("create")(os.fsencode(path), Bc.ctypes.data) if spmv else \
+            fn("create")(os.fsencode(path), Bc.ctypes.data, N)
+    if not h:
+        return {"unavailable": "reference loader or upload failed"}
+    try:
+        st = torch.cuda.current_stream()
+        sp = ctypes.c_void_p(st.cuda_stream)
+        fn("zero")(h, sp)
+        rc = fn("run")(h, sp)
+        if rc != 0:
+            return {"unavailable": f"reference kernel launch failed (cudaError {rc})"}
+        torch.cuda.synchronize()
+        out = np.zeros((m, N), np.float32)
+        fn("result")(h, out.ctypes.data)
+        ref = cpu.spmm_csr_float(ip, ix, dx, B)
+        scale = cpu.spmm_csr_abs(ip, ix, dx, B)
+        rel = float(np.max(np.abs(out.astype(np.float64) - ref) / np.maximum(scale, 1e-30)))
+        steps = max(3, min(args.steps, 20))
+        tot = 0.0
+        for _ in range(2):
+            fn("zero")(h, sp)
+            fn("run")(h, sp)
+        for _ in range(steps):
+            flush()
+            fn("zero")(h, sp)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(st)
+            fn("run")(h, sp)
+            e.record(st)
+            e.synchronize()
+            tot += s.elapsed_time(e)
+        ms = tot / steps
+        return {"value": 2.0 * len(ix) * N / (ms * 1e-3) / 1e9, "unit": "GFLOP/s", "kernel_us": ms * 1e3,
+                "coarsening": [4, kn], "max_err_over_abs_scale": rel,
+                "how": ("reference SpmvComplexPatternDecomposeByRowSeperated" if spmv else
+                        "reference SpMMFullRowPanelGeneralKernel4With2BlockCacheLess") +
+                       " built from its header for sm_100a (oracle/_ref), atomics into a zeroed C, CUDA events"}
+    finally:
+        fn("free")(h)
 
 
 def small_b_sweep(args):
@@ -707,6 +783,10 @@ def main():
     }
     if world == 1:
         line["cusparse"] = cusparse_baseline(mats, dev, flush, args)
+        try:
+            line["reference_gpu"] = reference_gpu_baseline(mats, flush, args)
+        except Exception as ex:  # reported baseline only
+            line["reference_gpu"] = {"unavailable": f"{type(ex).__name__}: {ex}"[:200]}
     if world == 1 and not args.no_cpu_baseline:
         g, kind, sample, dt = cpu_reference_rate(mats, args.cpu_seconds, 1)
         line["cpu_baseline"] = {"value": g, "unit": "GFLOP/s", "cores": 1, "kind": kind,

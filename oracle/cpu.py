@@ -19,7 +19,7 @@ _P = ctypes.c_void_p
 
 def build() -> None:
     """Runs the oracle Makefile (the _ref targets only when the reference tree exists)."""
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    subprocess.run(["make", "-s", "-j4", "-C", HERE], check=True)
 
 
 def _load(path, sigs):
@@ -133,6 +133,14 @@ def ref_lib(name):
             sigs = {"ref_spmm_csr_float": ([i, i, _P, _P, _P, _P, _P], None)}
         elif name == "libref_spmv.so":
             sigs = {"ref_spmv_csr_float": ([i, _P, _P, _P, _P, _P], None)}
+        elif name == "libref_gpu_spmm.so":
+            sigs = {"ref_gpu_spmm_create": ([ctypes.c_char_p, _P, i], _P), "ref_gpu_spmm_zero": ([_P, _P], i),
+                    "ref_gpu_spmm_run": ([_P, _P], i), "ref_gpu_spmm_result": ([_P, _P], i),
+                    "ref_gpu_spmm_free": ([_P], None)}
+        elif name == "libref_gpu_spmv.so":
+            sigs = {"ref_gpu_spmv_create": ([ctypes.c_char_p, _P], _P), "ref_gpu_spmv_zero": ([_P, _P], i),
+                    "ref_gpu_spmv_run": ([_P, _P], i), "ref_gpu_spmv_result": ([_P, _P], i),
+                    "ref_gpu_spmv_free": ([_P], None)}
         else:
             P64 = ctypes.POINTER(ctypes.c_int64)
             PP = ctypes.POINTER(ctypes.c_void_p)

@@ -84,6 +84,7 @@ def _build_locked(verbose: bool, force: bool) -> str:
             if verbose and out:
                 print(out)
     if force or jobs or not _newer(LIB, objs):
+        os.makedirs(os.path.dirname(LIB), exist_ok=True)
         tmp = f"{LIB}.tmp{os.getpid()}"  # renamed into place: a reader never sees a partial file
         _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-Xcompiler", "-fPIC", "-Xlinker",
               "--exclude-libs,ALL", *objs, "-o", tmp, "-lpthread"])

@@ -38,8 +38,14 @@ static sc::NarrowFn narrow_of(int nb) {
   }
 }
 
-// vt: 0 = fp32 records, 1 = fp16 compact records, 2 = bf16 compact records
+// vt: 0 = fp32 records, 1 = fp16 compact records, 2 = bf16 compact records,
+// 3 = split blocks (16-bit columns, fp32 values)
 sc::NarrowFn SC_CAT(sc_narrow_kernel_km, SC_KM)(int nb, int vt) {
-  return vt == 1 ? narrow_of<1>(nb) : (vt == 2 ? narrow_of<2>(nb) : narrow_of<0>(nb));
+  switch (vt) {
+    case 1: return narrow_of<1>(nb);
+    case 2: return narrow_of<2>(nb);
+    case 3: return narrow_of<3>(nb);
+    default: return narrow_of<0>(nb);
+  }
 }
 #endif

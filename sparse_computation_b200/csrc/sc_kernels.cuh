@@ -534,12 +534,56 @@ __device__ __forceinline__ void load_rec_any(const uint32_t *__restrict__ recs, 
   }
 }
 
+// Split item blocks (VT == 3, fp32 small-B plans with K <= 65536): an item of
+// `len` entries is [len 16-bit columns, zero-filled to 16 bytes][len * P fp32
+// values, zero-filled to 16 bytes], starting 16-byte aligned at word `off`.
+// 2 + 4P bytes per entry -- the interleaved fp32 record costs 8 bytes per
+// nonzero (column word and stride padding).
+__host__ __device__ constexpr uint32_t split_col_words(int len) { return (uint32_t)((len * 2 + 15) / 16) * 4u; }
+__host__ __device__ constexpr uint32_t split_val_words(int len, int p) { return (uint32_t)((len * p * 4 + 15) / 16) * 4u; }
+
+// Entry e of the item at `off` (len entries, popcount P): its column and values.
+template <int P, int VT>
+__device__ __forceinline__ void load_entry(const uint32_t *__restrict__ recs, uint32_t off, int len, int e, int &col,
+                                           float (&v)[P]) {
+  if constexpr (VT == 3) {
+    col = (int)__ldg(reinterpret_cast<const uint16_t *>(recs + off) + e);
+    const float *vals = reinterpret_cast<const float *>(recs + off + split_col_words(len)) + e * P;
+    if constexpr (P % 4 == 0) {
+#pragma unroll
+      for (int p = 0; p < P; p += 4) {
+        const float4 t = __ldg(reinterpret_cast<const float4 *>(vals + p));
+        v[p] = t.x; v[p + 1] = t.y; v[p + 2] = t.z; v[p + 3] = t.w;
+      }
+    } else if constexpr (P % 2 == 0) {
+#pragma unroll
+      for (int p = 0; p < P; p += 2) {
+        const float2 t = __ldg(reinterpret_cast<const float2 *>(vals + p));
+        v[p] = t.x; v[p + 1] = t.y;
+      }
+    } else {
+#pragma unroll
+      for (int p = 0; p < P; ++p) v[p] = __ldg(vals + p);
+    }
+  } else {
+    load_rec_any<P, VT>(recs, off + (uint32_t)(e * rec_stride(P)), col, v);
+  }
+}
+
+// Words of an item's records (from its first word), for the L2 prefetch.
+template <int VT>
+__device__ __forceinline__ uint32_t item_words(int2 item) {
+  const int len = item.y >> 16, P = __popc(item.y & 0xffff);
+  if constexpr (VT == 3) return split_col_words(len) + split_val_words(len, P);
+  const uint32_t units = (uint32_t)len * (P == 1 ? 2u : (P <= 3 ? 4u : 8u));
+  return VT == 0 ? units : (units + 1) / 2;
+}
+
 template <int KM, int MASK, int NB, int VT>
 __device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ recs, uint32_t off, int len,
                                            const float *__restrict__ B, int64_t ldb, int lane,
                                            float (&acc)[KM][NB]) {
   constexpr int P = popc_c(MASK);
-  constexpr int S = rec_stride(P);
   constexpr int U = kNarrowUnroll;
   for (int e0 = 0; e0 < len; e0 += 32 * U) {
     int col[U];
@@ -548,7 +592,7 @@ __device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ recs, ui
     for (int u = 0; u < U; ++u) {
       const int e = e0 + u * 32 + lane;
       if (e < len) {
-        load_rec_any<P, VT>(recs, off + (uint32_t)(e * S), col[u], v[u]);
+        load_entry<P, VT>(recs, off, len, e, col[u], v[u]);
       } else {
         col[u] = 0;  // row 0 of B, weight 0
 #pragma unroll
@@ -574,7 +618,6 @@ template <int KM, int P, int NB, int VT>
 __device__ __forceinline__ void seg_narrow_pc(const uint32_t *__restrict__ recs, uint32_t off, int len,
                                               const float *__restrict__ B, int64_t ldb, int lane, int mask,
                                               float (&acc)[KM][NB]) {
-  constexpr int S = rec_stride(P);
   constexpr int U = kNarrowUnroll;
   float t[P][NB];
 #pragma unroll
@@ -588,7 +631,7 @@ __device__ __forceinline__ void seg_narrow_pc(const uint32_t *__restrict__ recs,
     for (int u = 0; u < U; ++u) {
       const int e = e0 + u * 32 + lane;
       if (e < len) {
-        load_rec_any<P, VT>(recs, off + (uint32_t)(e * S), col[u], v[u]);
+        load_entry<P, VT>(recs, off, len, e, col[u], v[u]);
       } else {
         col[u] = 0;
 #pragma unroll
@@ -713,10 +756,10 @@ spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ i
   // latency instead of a chain of DRAM round trips.
   if (threadIdx.x == 0 && it1 > it0) {
     const int2 f = __ldg(items + it0), l = __ldg(items + it1 - 1);
-    const int pl = __popc(l.y & 0xffff);
-    const uint32_t end = (uint32_t)l.x + (uint32_t)((l.y >> 16) * (pl == 1 ? 2 : (pl <= 3 ? 4 : 8)));
-    constexpr uint32_t unit = VT == 0 ? 4u : 2u;
-    const uint32_t b0 = ((uint32_t)f.x * unit) & ~15u, b1 = (end * unit + 15u) & ~15u;
+    // item offsets count words (VT 0, 3) or halfwords (VT 1, 2)
+    constexpr uint32_t unit = (VT == 0 || VT == 3) ? 4u : 2u;
+    const uint32_t end_bytes = ((uint32_t)l.x * unit + item_words<VT>(l) * 4u);
+    const uint32_t b0 = ((uint32_t)f.x * unit) & ~15u, b1 = (end_bytes + 15u) & ~15u;
     const char *base = reinterpret_cast<const char *>(recs) + b0;
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base), "r"(b1 - b0) : "memory");
   }

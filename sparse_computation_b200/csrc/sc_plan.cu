@@ -85,7 +85,8 @@ struct sc_plan {
   int64_t dense_ntasks = 0;
   int dense_split = 1;          // CTAs (cluster) per task
   bool dense_bf16 = false;      // bf16 tiles (SC_PLAN_DENSE_BF16) instead of 3xTF32
-  int value_type = 0;           // records: 0 fp32, 1 compact fp16, 2 compact bf16 (small-B plans)
+  int value_type = 0;           // stored values: 0 fp32, 1 fp16, 2 bf16 (compact small-B records)
+  int record_vt = 0;            // record layout the narrow kernel reads: value_type, or 3 = split blocks
   uint32_t flags = 0;           // SC_PLAN_* given at creation
   ~sc_plan() {
     if (dev || stage_b || stage_c || a_tiles || chunk_order || side || khalf_items[0] || side2) {
@@ -160,6 +161,14 @@ NarrowFn narrow_kernel(int km, int nb, int vt) {
     case 5: return sc_narrow_kernel_km5(nb, vt);
     default: return sc_narrow_kernel_km6(nb, vt);
   }
+}
+
+bool split_records_enabled() {
+  static const bool v = [] {
+    const char *e = getenv("SC_SPLIT_RECORDS");
+    return !(e && e[0] == '0');
+  }();
+  return v;
 }
 
 int pow2_at_least(int64_t x) {
@@ -445,6 +454,11 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   plan->dense_bf16 = (flags & SC_PLAN_DENSE_BF16) != 0;
   plan->value_type = (flags & SC_PLAN_VALUES_F16) ? 1 : ((flags & SC_PLAN_VALUES_BF16) ? 2 : 0);
   const bool compact = plan->value_type != 0;
+  // fp32 small-B plans with K <= 65536: split item blocks (16-bit columns,
+  // then exactly P values per entry); SC_SPLIT_RECORDS=0 keeps the
+  // interleaved records (measurement switch).
+  const bool split = !compact && (n == 1 || n == 2 || n == 4) && cf.num_cols <= 65536 && split_records_enabled();
+  plan->record_vt = split ? 3 : plan->value_type;
   if (compact) {
     require(n == 1 || n == 2 || n == 4, SC_ERR_UNSUPPORTED,
             "16-bit value records are for the small-B / SpMV kernel (n_cols_b 1, 2 or 4)");
@@ -472,7 +486,22 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
       const int S = sc::rec_stride(P);
       int64_t seg_start = -1;
       int64_t seg_len = 0;
+      std::vector<uint32_t> seg_cols, seg_vals;  // split mode: the segment's columns and value bits
       auto close_items = [&]() {
+        if (split) {
+          for (int64_t e = 0; e < seg_len; e += item_cap) {
+            const int len = (int)std::min<int64_t>(item_cap, seg_len - e);
+            while (recs.size() % 4) recs.push_back(0);
+            const int64_t off = (int64_t)recs.size();
+            require(off < (int64_t)INT32_MAX, SC_ERR_UNSUPPORTED, "record stream exceeds 8 GiB");
+            for (int i = 0; i < len; i += 2)
+              recs.push_back(seg_cols[e + i] | (i + 1 < len ? seg_cols[e + i + 1] << 16 : 0u));
+            while (recs.size() % 4) recs.push_back(0);
+            recs.insert(recs.end(), seg_vals.begin() + e * P, seg_vals.begin() + (e + len) * P);
+            items.push_back(make_int2((int)off, rowbits[g] | (len << 16)));
+          }
+          return;
+        }
         for (int64_t e = 0; e < seg_len; e += item_cap) {
           int len = (int)std::min<int64_t>(item_cap, seg_len - e);
           int64_t off = seg_start + e * S;
@@ -486,6 +515,20 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
         if (all_pad) continue;
         const int32_t col = pt.cb[j];
         require(col >= 0 && col < cf.num_cols, SC_ERR_FORMAT, "column index out of range in CF");
+        if (split) {
+          seg_cols.push_back((uint32_t)col);
+          for (int p = 0; p < P; ++p) {
+            const float v = pt.vals[(size_t)j * P + p];
+            uint32_t w;
+            memcpy(&w, &v, 4);
+            seg_vals.push_back(w);
+            if (!pt.pad[(size_t)j * P + p]) plan->nnz++;
+          }
+          seg_len++;
+          plan->entries++;
+          work[lp] += P + 1;
+          continue;
+        }
         if (seg_start < 0) {
           // 16-byte aligned segment (8 words when compact: 16 bytes of halfwords)
           const size_t al = compact ? 8 : 4;
@@ -661,13 +704,13 @@ void launch_panels(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ld
   }
   if (p->kernel == 1) {
     if (ldb % nb == 0 && aligned(B, 4 * nb)) {
-      NarrowFn fn = narrow_kernel((int)p->km, nb, p->value_type);
+      NarrowFn fn = narrow_kernel((int)p->km, nb, p->record_vt);
       fn<<<dim3((unsigned)count), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, order, B, ldb, C, ldc,
                                                          p->rows, accumulate);
     } else {
       // B rows not aligned for an nb-wide vector load: one single-column
       // launch per column of B (scalar loads at any alignment)
-      NarrowFn fn = narrow_kernel((int)p->km, 1, p->value_type);
+      NarrowFn fn = narrow_kernel((int)p->km, 1, p->record_vt);
       for (int q = 0; q < nb; ++q)
         fn<<<dim3((unsigned)count), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, order, B + q, ldb,
                                                            C + q, ldc, p->rows, accumulate);
@@ -698,7 +741,9 @@ bool host_ksplit_enabled() {
 // One half of a K-split wide product over all panels: half 0 writes
 // C = A[:, :ksplit] B[:ksplit]; half 1 adds A[:, ksplit:] B[ksplit:] to it and,
 // when `host_c` is given, stores the finished tiles there as well.
-void launch_khalf(sc_plan *p, int h, float *C, float *host_c, cudaStream_t stream) {
+void launch_khalf(sc_plan *p, int h, float *C, float *host_c, cudaStream_t stream, const int32_t *order,
+                  int64_t count) {
+  if (count <= 0) return;
   int vec = p->vec;
   while (vec > 1 && (p->n % vec != 0 || (host_c && !aligned(host_c, 4 * vec)))) vec >>= 1;
   const int slices = (int)((p->n + 32 * vec - 1) / (32 * vec));
@@ -711,7 +756,7 @@ void launch_khalf(sc_plan *p, int h, float *C, float *host_c, cudaStream_t strea
   }
   WideFn fn = wide_kernel((int)p->km, vec, false);
   const size_t smem = sc::wide_smem_bytes(p->warps, (int)p->km, vec);
-  fn<<<dim3((unsigned)p->panels, slices), 32 * p->warps, smem, stream>>>(a, nullptr, p->order, h);
+  fn<<<dim3((unsigned)count, slices), 32 * p->warps, smem, stream>>>(a, nullptr, order, h);
   cuda_check(cudaGetLastError(), "kernel launch");
 }
 
@@ -929,10 +974,14 @@ int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream) {
     copy(3, p->side2);
     cuda_check(cudaEventRecord(ev[4], p->side2), "record event");
     cuda_check(cudaStreamWaitEvent(s, ev[2], 0), "wait event");
-    launch_khalf(p, 0, p->stage_c, nullptr, s);
+    launch_khalf(p, 0, p->stage_c, nullptr, s, p->order, p->panels);
     cuda_check(cudaStreamWaitEvent(s, ev[3], 0), "wait event");
     cuda_check(cudaStreamWaitEvent(s, ev[4], 0), "wait event");
-    launch_khalf(p, 1, p->stage_c, dC_host, s);
+    // One launch: the row-chunked alternative (C of one chunk crossing the
+    // host link while the next computes) measured slower on config 5 --
+    // 508 us whole, 583 / 734 / 1062 us in 2 / 4 / 8 chunks -- since each
+    // chunk alone is a thin, latency-bound wave.
+    launch_khalf(p, 1, p->stage_c, dC_host, s, p->order, p->panels);
     cuda_check(cudaStreamSynchronize(s), "stream synchronize");
     return SC_OK;  // wide plan: no device-side waits
   }

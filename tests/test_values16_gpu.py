@@ -96,7 +96,10 @@ def test_16bit_values_smaller_records(cuda):
     p32 = sc.SpMMPlan(cf, 4)
     p16 = sc.SpMMPlan(cf, 4, flags=sc.SC_PLAN_VALUES_F16)
     assert p16.info["entries"] == p32.info["entries"] and p16.info["nnz"] == p32.info["nnz"]
-    assert p16.info["device_bytes"] < 0.6 * p32.info["device_bytes"]
+    # fp32 small-B plans use split item blocks (2 + 4P bytes per entry, below
+    # the interleaved 8 bytes per nonzero); 16-bit records are smaller still
+    assert p32.info["device_bytes"] < 8 * p32.info["nnz"]
+    assert p16.info["device_bytes"] < 0.8 * p32.info["device_bytes"]
 
 
 def test_16bit_values_rejections(cuda):
