@@ -17,9 +17,31 @@ REF_DIR = os.path.join(HERE, "_ref")
 _P = ctypes.c_void_p
 
 
-def build() -> None:
-    """Runs the oracle Makefile (the _ref targets only when the reference tree exists)."""
-    subprocess.run(["make", "-s", "-j4", "-C", HERE], check=True)
+REF_SOURCE_FILE = os.path.join(REF_DIR, "source_dir.txt")
+
+
+def reference_dir() -> str:
+    """The reference checkout: SC_REFERENCE_DIR, else the one the last build
+    compiled oracle/_ref from ("" when neither exists)."""
+    d = os.environ.get("SC_REFERENCE_DIR", "")
+    if not d and os.path.exists(REF_SOURCE_FILE):
+        d = open(REF_SOURCE_FILE).read().strip()
+    return d if d and os.path.isdir(d) else ""
+
+
+def build(ref_dir: str = "") -> None:
+    """Runs the oracle Makefile; the _ref targets only when a reference
+    checkout is given (argument or SC_REFERENCE_DIR), whose location is then
+    recorded for the tests that read the reference's fixtures."""
+    ref = ref_dir or os.environ.get("SC_REFERENCE_DIR", "")
+    cmd = ["make", "-s", "-j4", "-C", HERE]
+    if ref and os.path.isdir(ref):
+        cmd.append(f"REF={ref}")
+    subprocess.run(cmd, check=True)
+    if ref and os.path.isdir(ref):
+        os.makedirs(REF_DIR, exist_ok=True)
+        with open(REF_SOURCE_FILE, "w") as f:
+            f.write(os.path.abspath(ref) + "\n")
 
 
 def _load(path, sigs):

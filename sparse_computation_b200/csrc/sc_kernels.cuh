@@ -101,22 +101,30 @@ __device__ __forceinline__ void load_b(const float *p, float (&out)[VEC]) {
 #endif
 }
 
+// Read-only load: through the non-coherent global path, or a plain load
+// when SM (the data was staged in shared memory).
+template <bool SM, typename T>
+__device__ __forceinline__ T ldro(const T *p) {
+  if constexpr (SM) return *p;
+  else return __ldg(p);
+}
+
 // Loads one record (column + P values) at `r`.
-template <int P>
+template <int P, bool SM = false>
 __device__ __forceinline__ void load_rec(const uint32_t *__restrict__ r, int &col, float (&v)[P]) {
   constexpr int S = rec_stride(P);
   if constexpr (S == 2) {
-    uint2 t = __ldg(reinterpret_cast<const uint2 *>(r));
+    uint2 t = ldro<SM>(reinterpret_cast<const uint2 *>(r));
     col = (int)t.x; v[0] = __uint_as_float(t.y);
   } else if constexpr (S == 4) {
-    uint4 t = __ldg(reinterpret_cast<const uint4 *>(r));
+    uint4 t = ldro<SM>(reinterpret_cast<const uint4 *>(r));
     col = (int)t.x;
     uint32_t w[3] = {t.y, t.z, t.w};
 #pragma unroll
     for (int p = 0; p < P; ++p) v[p] = __uint_as_float(w[p]);
   } else {
-    uint4 a = __ldg(reinterpret_cast<const uint4 *>(r));
-    uint4 b = __ldg(reinterpret_cast<const uint4 *>(r) + 1);
+    uint4 a = ldro<SM>(reinterpret_cast<const uint4 *>(r));
+    uint4 b = ldro<SM>(reinterpret_cast<const uint4 *>(r) + 1);
     col = (int)a.x;
     uint32_t w[7] = {a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -247,12 +255,29 @@ __device__ __forceinline__ void seg_wide(const uint32_t *rbuf, int len, const ch
   for (int e0 = 0; e0 < len; e0 += U) {
     float v[U][P];
     float b[U][VEC];
+    uint32_t col[U];
+    if constexpr (S == 2 && U % 2 == 0) {
+      // two 8-byte records per 16-byte broadcast load (one shared-memory
+      // wavefront instead of two); the pair index is clamped into the item,
+      // and a pair's second record past an odd length is the segment's zero
+      // fill (copied with the item's last 16-byte chunk)
+#pragma unroll
+      for (int u = 0; u < U; u += 2) {
+        const int e = min(e0 + u, (len - 1) & ~1);
+        const uint4 t = *reinterpret_cast<const uint4 *>(rbuf + e * 2);
+        col[u] = t.x;
+        v[u][0] = __uint_as_float(t.y);
+        col[u + 1] = t.z;
+        v[u + 1][0] = __uint_as_float(t.w);
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) lds_rec<P>(rbuf + min(e0 + u, len - 1) * S, col[u], v[u]);
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      uint32_t col;
-      lds_rec<P>(rbuf + min(e0 + u, len - 1) * S, col, v[u]);
       if (active && e0 + u < len) {
-        load_b<VEC>(reinterpret_cast<const float *>(Bcol + (uint64_t)col * ldb_bytes), b[u]);
+        load_b<VEC>(reinterpret_cast<const float *>(Bcol + (uint64_t)col[u] * ldb_bytes), b[u]);
       } else {
 #pragma unroll
         for (int q = 0; q < VEC; ++q) b[u][q] = 0.f;
@@ -507,22 +532,22 @@ static __global__ void wait_flags_kernel(const int *flags, int n, int epoch, int
 // l, l+32, l+64, l+96 and issues all their record loads, then all their B
 // loads, before the FMAs -- four independent DRAM requests per lane in
 // flight, and the item's mask dispatch paid once per 128 entries.
-template <int P, int VT>
+template <int P, int VT, bool SM>
 __device__ __forceinline__ void load_rec_any(const uint32_t *__restrict__ recs, uint32_t off, int &col,
                                              float (&v)[P]) {
   constexpr int S = rec_stride(P);
   if constexpr (VT == 0) {
-    load_rec<P>(recs + off, col, v);
+    load_rec<P, SM>(recs + off, col, v);
   } else {
     const uint16_t *r = reinterpret_cast<const uint16_t *>(recs) + off;
     uint32_t w[4] = {0u, 0u, 0u, 0u};
     if constexpr (S == 2) {
-      w[0] = __ldg(reinterpret_cast<const uint32_t *>(r));
+      w[0] = ldro<SM>(reinterpret_cast<const uint32_t *>(r));
     } else if constexpr (S == 4) {
-      const uint2 t = __ldg(reinterpret_cast<const uint2 *>(r));
+      const uint2 t = ldro<SM>(reinterpret_cast<const uint2 *>(r));
       w[0] = t.x; w[1] = t.y;
     } else {
-      const uint4 t = __ldg(reinterpret_cast<const uint4 *>(r));
+      const uint4 t = ldro<SM>(reinterpret_cast<const uint4 *>(r));
       w[0] = t.x; w[1] = t.y; w[2] = t.z; w[3] = t.w;
     }
     col = (int)(w[0] & 0xffffu);
@@ -543,30 +568,30 @@ __host__ __device__ constexpr uint32_t split_col_words(int len) { return (uint32
 __host__ __device__ constexpr uint32_t split_val_words(int len, int p) { return (uint32_t)((len * p * 4 + 15) / 16) * 4u; }
 
 // Entry e of the item at `off` (len entries, popcount P): its column and values.
-template <int P, int VT>
+template <int P, int VT, bool SM>
 __device__ __forceinline__ void load_entry(const uint32_t *__restrict__ recs, uint32_t off, int len, int e, int &col,
                                            float (&v)[P]) {
   if constexpr (VT == 3) {
-    col = (int)__ldg(reinterpret_cast<const uint16_t *>(recs + off) + e);
+    col = (int)ldro<SM>(reinterpret_cast<const uint16_t *>(recs + off) + e);
     const float *vals = reinterpret_cast<const float *>(recs + off + split_col_words(len)) + e * P;
     if constexpr (P % 4 == 0) {
 #pragma unroll
       for (int p = 0; p < P; p += 4) {
-        const float4 t = __ldg(reinterpret_cast<const float4 *>(vals + p));
+        const float4 t = ldro<SM>(reinterpret_cast<const float4 *>(vals + p));
         v[p] = t.x; v[p + 1] = t.y; v[p + 2] = t.z; v[p + 3] = t.w;
       }
     } else if constexpr (P % 2 == 0) {
 #pragma unroll
       for (int p = 0; p < P; p += 2) {
-        const float2 t = __ldg(reinterpret_cast<const float2 *>(vals + p));
+        const float2 t = ldro<SM>(reinterpret_cast<const float2 *>(vals + p));
         v[p] = t.x; v[p + 1] = t.y;
       }
     } else {
 #pragma unroll
-      for (int p = 0; p < P; ++p) v[p] = __ldg(vals + p);
+      for (int p = 0; p < P; ++p) v[p] = ldro<SM>(vals + p);
     }
   } else {
-    load_rec_any<P, VT>(recs, off + (uint32_t)(e * rec_stride(P)), col, v);
+    load_rec_any<P, VT, SM>(recs, off + (uint32_t)(e * rec_stride(P)), col, v);
   }
 }
 
@@ -579,7 +604,7 @@ __device__ __forceinline__ uint32_t item_words(int2 item) {
   return VT == 0 ? units : (units + 1) / 2;
 }
 
-template <int KM, int MASK, int NB, int VT>
+template <int KM, int MASK, int NB, int VT, bool SM>
 __device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ recs, uint32_t off, int len,
                                            const float *__restrict__ B, int64_t ldb, int lane,
                                            float (&acc)[KM][NB]) {
@@ -592,7 +617,7 @@ __device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ recs, ui
     for (int u = 0; u < U; ++u) {
       const int e = e0 + u * 32 + lane;
       if (e < len) {
-        load_entry<P, VT>(recs, off, len, e, col[u], v[u]);
+        load_entry<P, VT, SM>(recs, off, len, e, col[u], v[u]);
       } else {
         col[u] = 0;  // row 0 of B, weight 0
 #pragma unroll
@@ -614,7 +639,7 @@ __device__ __forceinline__ void seg_narrow(const uint32_t *__restrict__ recs, ui
 
 // Popcount-class body of the narrow kernel (kernel_m above SC_MASK_KM_MAX);
 // see seg_wide_pc.
-template <int KM, int P, int NB, int VT>
+template <int KM, int P, int NB, int VT, bool SM>
 __device__ __forceinline__ void seg_narrow_pc(const uint32_t *__restrict__ recs, uint32_t off, int len,
                                               const float *__restrict__ B, int64_t ldb, int lane, int mask,
                                               float (&acc)[KM][NB]) {
@@ -631,7 +656,7 @@ __device__ __forceinline__ void seg_narrow_pc(const uint32_t *__restrict__ recs,
     for (int u = 0; u < U; ++u) {
       const int e = e0 + u * 32 + lane;
       if (e < len) {
-        load_entry<P, VT>(recs, off, len, e, col[u], v[u]);
+        load_entry<P, VT, SM>(recs, off, len, e, col[u], v[u]);
       } else {
         col[u] = 0;
 #pragma unroll
@@ -651,38 +676,38 @@ __device__ __forceinline__ void seg_narrow_pc(const uint32_t *__restrict__ recs,
   add_rows<KM, P, NB>(mask, t, acc);
 }
 
-template <int KM, int NB, int VT, int LO, int HI>
+template <int KM, int NB, int VT, bool SM, int LO, int HI>
 __device__ __forceinline__ void dispatch_narrow_mask(int mask, const uint32_t *__restrict__ recs, uint32_t off,
                                                      int len, const float *__restrict__ B, int64_t ldb, int lane,
                                                      float (&acc)[KM][NB]) {
   if constexpr (HI - LO == 1) {
-    seg_narrow<KM, LO, NB, VT>(recs, off, len, B, ldb, lane, acc);
+    seg_narrow<KM, LO, NB, VT, SM>(recs, off, len, B, ldb, lane, acc);
   } else {
     constexpr int MID = (LO + HI) / 2;
-    if (mask < MID) dispatch_narrow_mask<KM, NB, VT, LO, MID>(mask, recs, off, len, B, ldb, lane, acc);
-    else dispatch_narrow_mask<KM, NB, VT, MID, HI>(mask, recs, off, len, B, ldb, lane, acc);
+    if (mask < MID) dispatch_narrow_mask<KM, NB, VT, SM, LO, MID>(mask, recs, off, len, B, ldb, lane, acc);
+    else dispatch_narrow_mask<KM, NB, VT, SM, MID, HI>(mask, recs, off, len, B, ldb, lane, acc);
   }
 }
 
-template <int KM, int NB, int VT, int LO, int HI>
+template <int KM, int NB, int VT, bool SM, int LO, int HI>
 __device__ __forceinline__ void dispatch_narrow_pc(int mask, const uint32_t *__restrict__ recs, uint32_t off,
                                                    int len, const float *__restrict__ B, int64_t ldb, int lane,
                                                    float (&acc)[KM][NB]) {
   if constexpr (HI - LO == 1) {
-    seg_narrow_pc<KM, LO, NB, VT>(recs, off, len, B, ldb, lane, mask, acc);
+    seg_narrow_pc<KM, LO, NB, VT, SM>(recs, off, len, B, ldb, lane, mask, acc);
   } else {
     constexpr int MID = (LO + HI) / 2;
-    if (__popc(mask) < MID) dispatch_narrow_pc<KM, NB, VT, LO, MID>(mask, recs, off, len, B, ldb, lane, acc);
-    else dispatch_narrow_pc<KM, NB, VT, MID, HI>(mask, recs, off, len, B, ldb, lane, acc);
+    if (__popc(mask) < MID) dispatch_narrow_pc<KM, NB, VT, SM, LO, MID>(mask, recs, off, len, B, ldb, lane, acc);
+    else dispatch_narrow_pc<KM, NB, VT, SM, MID, HI>(mask, recs, off, len, B, ldb, lane, acc);
   }
 }
 
-template <int KM, int NB, int VT>
+template <int KM, int NB, int VT, bool SM>
 __device__ __forceinline__ void dispatch_narrow(int mask, const uint32_t *__restrict__ recs, uint32_t off, int len,
                                                 const float *__restrict__ B, int64_t ldb, int lane,
                                                 float (&acc)[KM][NB]) {
-  if constexpr (KM <= SC_MASK_KM_MAX) dispatch_narrow_mask<KM, NB, VT, 1, (1 << KM)>(mask, recs, off, len, B, ldb, lane, acc);
-  else dispatch_narrow_pc<KM, NB, VT, 1, KM + 1>(mask, recs, off, len, B, ldb, lane, acc);
+  if constexpr (KM <= SC_MASK_KM_MAX) dispatch_narrow_mask<KM, NB, VT, SM, 1, (1 << KM)>(mask, recs, off, len, B, ldb, lane, acc);
+  else dispatch_narrow_pc<KM, NB, VT, SM, 1, KM + 1>(mask, recs, off, len, B, ldb, lane, acc);
 }
 
 __host__ __device__ constexpr int pow2_ceil(int x) {
@@ -770,7 +795,7 @@ spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ i
     const int2 mine = lane < cnt ? __ldg(items + it0 + warp + (base + lane) * nw) : make_int2(0, 0);
     for (int j = 0; j < cnt; ++j) {
       const int2 item = make_int2(__shfl_sync(0xffffffffu, mine.x, j), __shfl_sync(0xffffffffu, mine.y, j));
-      dispatch_narrow<KM, NB, VT>(item.y & 0xffff, recs, (uint32_t)item.x, item.y >> 16, B, ldb,
+      dispatch_narrow<KM, NB, VT, false>(item.y & 0xffff, recs, (uint32_t)item.x, item.y >> 16, B, ldb,
                                                 lane, acc);
     }
   }
@@ -794,6 +819,140 @@ spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ i
   }
 }
 
+// ------------------------------------------------ narrow B, bulk-staged ----
+// The same product as spmm_narrow_kernel, with the records of the CTA's
+// panel pulled into shared memory by the bulk-copy engine
+// (cp.async.bulk.shared::cluster.global, mbarrier completion) in chunks of
+// whole items of at most kBulkBytes, double-buffered: the next chunk is in
+// flight while the warps compute on the current one.  Per-lane 2- to 16-byte
+// record loads leave too few bytes in flight to cover DRAM latency (config-5
+// SpMV: latency-bound at ~0.25 of HBM); one 16 KiB request per CTA does not.
+// chunks[c] = {first item, end item, first 16-byte unit, bytes}; the chunks of local
+// panel i are [chunk_ptr[i], chunk_ptr[i+1]).  Every wait is bounded: on
+// expiry the CTA writes 6 into *status, waits (bounded) for its copies in
+// flight, skips its C stores and returns.
+constexpr int kBulkBytes = 16384;
+constexpr uint32_t kBulkWaitLimit = 1u << 20;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ bool bulk_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool bulk_wait(uint64_t *bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kBulkWaitLimit; ++i)
+    if (bulk_try_wait(bar, parity)) return true;
+  return false;
+}
+
+template <int KM, int NB, int VT>
+__global__ void __launch_bounds__(128)
+spmm_narrow_bulk_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ items,
+                        const int4 *__restrict__ chunks, const int32_t *__restrict__ chunk_ptr,
+                        const int32_t *__restrict__ order, const float *__restrict__ B, int64_t ldb,
+                        float *__restrict__ C, int64_t ldc, int64_t rows, int accumulate, int *status) {
+  constexpr int V = pow2_ceil(KM * NB);
+  static_assert(V <= 32, "KM*NB must not exceed 32");
+  extern __shared__ __align__(128) uint32_t sbuf[];  // 2 x kBulkBytes
+  __shared__ __align__(8) uint64_t full[2];
+  __shared__ float red[4][V];
+  __shared__ int failed;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const int panel = order[blockIdx.x];
+  const int c0 = chunk_ptr[panel], nc = chunk_ptr[panel + 1] - c0;
+
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[0])) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[1])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    failed = 0;
+  }
+  __syncthreads();
+  auto issue = [&](int k) {  // thread 0: chunk k into buffer k & 1
+    const int4 ch = __ldg(chunks + c0 + k);
+    uint64_t *bar = &full[k & 1];
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(ch.w)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(reinterpret_cast<char *>(sbuf) + (k & 1) * kBulkBytes)),
+        "l"(reinterpret_cast<const char *>(recs) + (uint64_t)(uint32_t)ch.z * 16u), "r"(ch.w), "r"(smem_addr(bar))
+        : "memory");
+  };
+  if (threadIdx.x == 0) {
+    if (nc > 0) issue(0);
+    if (nc > 1) issue(1);
+  }
+
+  float acc[KM][NB];
+#pragma unroll
+  for (int k = 0; k < KM; ++k)
+#pragma unroll
+    for (int q = 0; q < NB; ++q) acc[k][q] = 0.f;
+
+  int k = 0;
+  for (; k < nc; ++k) {
+    if (!bulk_wait(&full[k & 1], (k >> 1) & 1)) {
+      failed = 1;  // benign race: every writer stores 1
+    }
+    __syncthreads();
+    if (failed) break;
+    const int4 ch = __ldg(chunks + c0 + k);
+    // the chunk's records sit in buffer k & 1 from its first 16-byte unit
+    // ch.z on; item offsets count words (VT 0, 3) or halfwords (VT 1, 2)
+    const uint32_t *buf = sbuf + (k & 1) * (kBulkBytes / 4);
+    constexpr int kUnitsPer16 = (VT == 1 || VT == 2) ? 8 : 4;
+    const uint32_t first = (uint32_t)ch.z * kUnitsPer16;
+    for (int it = ch.x + warp; it < ch.y; it += nw) {
+      const int2 item = __ldg(items + it);
+      dispatch_narrow<KM, NB, VT, true>(item.y & 0xffff, buf, (uint32_t)item.x - first, item.y >> 16, B, ldb, lane,
+                                        acc);
+    }
+    __syncthreads();  // buffer k & 1 consumed
+    if (threadIdx.x == 0 && k + 2 < nc) issue(k + 2);
+  }
+  if (failed) {
+    // wait (bounded) for this CTA's copies still in flight, then leave C alone
+    if (threadIdx.x == 0) {
+      atomicExch(status, 6);
+      for (int j = k; j < nc && j < k + 2; ++j) bulk_wait(&full[j & 1], (j >> 1) & 1);
+    }
+    return;
+  }
+
+  float v[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) v[i] = (i < KM * NB) ? acc[i / NB][i % NB] : 0.f;
+  warp_transpose_reduce<V>(v, lane);
+  constexpr int kRep = 32 / V;
+  if ((lane % kRep) == 0) red[warp][transpose_reduce_index<V>(lane)] = v[0];
+  __syncthreads();
+  if (threadIdx.x < KM * NB) {
+    float sum = 0.f;
+    for (int w = 0; w < nw; ++w) sum += red[w][threadIdx.x];
+    const int kk = threadIdx.x / NB, q = threadIdx.x % NB;
+    const int64_t row = (int64_t)panel * KM + kk;
+    if (row < rows) {
+      float *c = C + row * ldc + q;
+      *c = accumulate ? *c + sum : sum;
+    }
+  }
+}
+
+using NarrowBulkFn = void (*)(const uint32_t *, const int2 *, const int4 *, const int32_t *, const int32_t *,
+                              const float *, int64_t, float *, int64_t, int64_t, int, int *);
+
 using WideFn = void (*)(WideArgs, const WideArgs *, const int32_t *, int);
 using NarrowFn = void (*)(const uint32_t *, const int2 *, const int32_t *, const int32_t *, const float *,
                           int64_t, float *, int64_t, int64_t, int);
@@ -813,3 +972,9 @@ sc::NarrowFn sc_narrow_kernel_km3(int nb, int vt);
 sc::NarrowFn sc_narrow_kernel_km4(int nb, int vt);
 sc::NarrowFn sc_narrow_kernel_km5(int nb, int vt);
 sc::NarrowFn sc_narrow_kernel_km6(int nb, int vt);
+sc::NarrowBulkFn sc_narrow_bulk_kernel_km1(int nb, int vt);
+sc::NarrowBulkFn sc_narrow_bulk_kernel_km2(int nb, int vt);
+sc::NarrowBulkFn sc_narrow_bulk_kernel_km3(int nb, int vt);
+sc::NarrowBulkFn sc_narrow_bulk_kernel_km4(int nb, int vt);
+sc::NarrowBulkFn sc_narrow_bulk_kernel_km5(int nb, int vt);
+sc::NarrowBulkFn sc_narrow_bulk_kernel_km6(int nb, int vt);

@@ -7,7 +7,11 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-REFERENCE = "/root/reference"  # present only in the build container, never on GPU boxes
+from oracle import cpu as _cpu  # noqa: E402
+
+# The reference checkout (SC_REFERENCE_DIR, else where the build found it); it
+# exists only where the library was built, never on GPU boxes.
+REFERENCE = _cpu.reference_dir()
 
 
 def pytest_configure(config):
@@ -28,7 +32,7 @@ def _built():
 
 
 def has_reference() -> bool:
-    return os.path.isdir(os.path.join(REFERENCE, "code_gen"))
+    return bool(REFERENCE) and os.path.isdir(os.path.join(REFERENCE, "code_gen"))
 
 
 @pytest.fixture(scope="session")

@@ -24,7 +24,9 @@ sys.path.insert(0, ROOT)
 from sparse_computation_b200 import workloads as wl  # noqa: E402
 from oracle import cpu  # noqa: E402
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else cpu.reference_dir()
+if not REF:
+    sys.exit("usage: make_golden.py <reference checkout> (or set SC_REFERENCE_DIR)")
 CONVERTER = os.path.join(REF, "code_gen", "ss_format", "format_generator.py")
 
 

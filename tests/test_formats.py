@@ -176,7 +176,6 @@ def test_float_repr_matches_python(tmp_path):
     vals += [float(np.float32(rng.gauss(0, 1) * 10 ** rng.randint(-30, 30))) for _ in range(3000)]
     vals = [v for v in vals if np.isfinite(v)]
     m = len(vals)
-    a = wl.CSRArrays if False else None
     ip = np.arange(m + 1, dtype=np.int32)
     ix = np.zeros(m, np.int32)
     cf = sc.csr_to_compressed_format_converter(sc.CSR.from_arrays(m, 1, ip, ix, np.array(vals)), 1, 1)
