@@ -66,6 +66,8 @@ def parse():
     p.add_argument("--values", choices=["f32", "f16", "bf16"], default="f32",
                    help="opt-in: small-B / SpMV plans (N in {1,2,4}) with A's values stored in 16 bits "
                         "(fp32 products and sums, looser error bound); the default and the reference use fp32")
+    p.add_argument("--no-graph", action="store_true",
+                   help="config 4: launch the batch directly instead of replaying its captured CUDA graph")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU work of the bounded cpu_baseline sample")
     return p.parse_args()
@@ -365,8 +367,10 @@ def reference_gpu_baseline(mats, flush, args):
     if not h:
         return {"unavailable": "reference loader or upload failed"}
     try:
-        st = torch.cuda.current_stream()
-        sp = ctypes.c_void_p(st.cuda_stream)
+        # the reference library carries its own CUDA runtime: it launches on the
+        # legacy default stream (as the reference does), timed on that stream
+        st = torch.cuda.default_stream()
+        sp = None
         fn("zero")(h, sp)
         rc = fn("run")(h, sp)
         if rc != 0:
@@ -587,6 +591,11 @@ def main():
             bt = sc.SpMMBatch([j["plan"] for j in grp])
             bt.bind([j["B"] for j in grp], [j["C"] for j in grp])
             batches.append(bt)
+    # config 4: each GPU's whole layer-stack product captured once into a CUDA
+    # graph and replayed (one graph launch per step)
+    graphs = []
+    if layers and batches and not args.no_graph:
+        graphs = [bt.capture(repeat=1) for bt in batches]
     t_setup = time.perf_counter() - t_setup
 
     peer_mode = world > 1 and not layers and args.exchange.startswith("peer")
@@ -594,7 +603,10 @@ def main():
     epoch = [0]
 
     def launch_all(stream):
-        if batches:
+        if graphs:
+            for g in graphs:
+                g.launch(stream=stream)
+        elif batches:
             for bt in batches:
                 bt.spmm(stream=stream)  # every local matrix of one kernel_m in one kernel launch
         else:
@@ -763,6 +775,7 @@ def main():
                                     "NVLink (symmetric memory) + one barrier" if peer_mode else
                                     f"row-partition x{world} + NCCL all-gather of C")),
                    "launches_per_step": len(batches) if batches else len(jobs),
+                   "cuda_graph": bool(graphs),
                    "l2": "flushed before every timed step (256 MiB write, then a 256 MiB read of another buffer so the "
                          "flush's dirty lines are written back; outside the events)",
                    "plan": {k: info[k] for k in ("entries", "items", "kernel", "warps_per_panel",

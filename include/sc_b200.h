@@ -219,10 +219,9 @@ int sc_spmm_host(sc_plan *p, const float *hB, float *hC, void *stream);
  * for all work on the plan's device (cudaDeviceSynchronize), copies the
  * plan's status word to *status and clears it.  0 = no error; 1, 2, 3 = a
  * bounded mbarrier wait of the dense-tile kernel expired (producer, MMA
- * issuer, epilogue) and that CTA skipped its C stores; 6 = a bounded wait
- * for a bulk copy of the small-B kernel expired (that panel's C rows were not
- * written).  Wide-B plans have no waits inside their kernel and always report
- * 0.  sc_spmm_host checks it itself and returns SC_ERR_DEVICE.
+ * issuer, epilogue) and that CTA skipped its C stores.  Only dense-tile
+ * plans (sc_plan_info.kernel == 3) wait inside their kernel; other plans
+ * always report 0.  sc_spmm_host checks it itself and returns SC_ERR_DEVICE.
  * The reference checks no kernel status (example_cuda/spmm_demo_gpu_utils.h:16-23
  * checks launch errors only). */
 int sc_plan_status(sc_plan *p, int32_t *status);

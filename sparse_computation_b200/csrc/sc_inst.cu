@@ -38,24 +38,6 @@ static sc::NarrowFn narrow_of(int nb) {
   }
 }
 
-template <int VT>
-static sc::NarrowBulkFn narrow_bulk_of(int nb) {
-  switch (nb) {
-    case 1: return sc::spmm_narrow_bulk_kernel<SC_KM, 1, VT>;
-    case 2: return sc::spmm_narrow_bulk_kernel<SC_KM, 2, VT>;
-    default: return sc::spmm_narrow_bulk_kernel<SC_KM, 4, VT>;
-  }
-}
-
-sc::NarrowBulkFn SC_CAT(sc_narrow_bulk_kernel_km, SC_KM)(int nb, int vt) {
-  switch (vt) {
-    case 1: return narrow_bulk_of<1>(nb);
-    case 2: return narrow_bulk_of<2>(nb);
-    case 3: return narrow_bulk_of<3>(nb);
-    default: return narrow_bulk_of<0>(nb);
-  }
-}
-
 // vt: 0 = fp32 records, 1 = fp16 compact records, 2 = bf16 compact records,
 // 3 = split blocks (16-bit columns, fp32 values)
 sc::NarrowFn SC_CAT(sc_narrow_kernel_km, SC_KM)(int nb, int vt) {

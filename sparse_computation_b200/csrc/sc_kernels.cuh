@@ -45,7 +45,10 @@ namespace sc {
 #endif
 
 constexpr int kItemEntries = 32;        // wide kernel: entries per item
-constexpr int kNarrowUnroll = 4;        // narrow kernel: entries per lane per pass
+#ifndef SC_NARROW_UNROLL
+#define SC_NARROW_UNROLL 4
+#endif
+constexpr int kNarrowUnroll = SC_NARROW_UNROLL;  // narrow kernel: entries per lane per pass
 constexpr int kNarrowItemEntries = 32 * kNarrowUnroll;
 
 __host__ __device__ constexpr int popc_c(int x) {
@@ -819,140 +822,6 @@ spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ i
   }
 }
 
-// ------------------------------------------------ narrow B, bulk-staged ----
-// The same product as spmm_narrow_kernel, with the records of the CTA's
-// panel pulled into shared memory by the bulk-copy engine
-// (cp.async.bulk.shared::cluster.global, mbarrier completion) in chunks of
-// whole items of at most kBulkBytes, double-buffered: the next chunk is in
-// flight while the warps compute on the current one.  Per-lane 2- to 16-byte
-// record loads leave too few bytes in flight to cover DRAM latency (config-5
-// SpMV: latency-bound at ~0.25 of HBM); one 16 KiB request per CTA does not.
-// chunks[c] = {first item, end item, first 16-byte unit, bytes}; the chunks of local
-// panel i are [chunk_ptr[i], chunk_ptr[i+1]).  Every wait is bounded: on
-// expiry the CTA writes 6 into *status, waits (bounded) for its copies in
-// flight, skips its C stores and returns.
-constexpr int kBulkBytes = 16384;
-constexpr uint32_t kBulkWaitLimit = 1u << 20;
-
-__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ bool bulk_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ bool bulk_wait(uint64_t *bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kBulkWaitLimit; ++i)
-    if (bulk_try_wait(bar, parity)) return true;
-  return false;
-}
-
-template <int KM, int NB, int VT>
-__global__ void __launch_bounds__(128)
-spmm_narrow_bulk_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ items,
-                        const int4 *__restrict__ chunks, const int32_t *__restrict__ chunk_ptr,
-                        const int32_t *__restrict__ order, const float *__restrict__ B, int64_t ldb,
-                        float *__restrict__ C, int64_t ldc, int64_t rows, int accumulate, int *status) {
-  constexpr int V = pow2_ceil(KM * NB);
-  static_assert(V <= 32, "KM*NB must not exceed 32");
-  extern __shared__ __align__(128) uint32_t sbuf[];  // 2 x kBulkBytes
-  __shared__ __align__(8) uint64_t full[2];
-  __shared__ float red[4][V];
-  __shared__ int failed;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int nw = blockDim.x >> 5;
-  const int panel = order[blockIdx.x];
-  const int c0 = chunk_ptr[panel], nc = chunk_ptr[panel + 1] - c0;
-
-  if (threadIdx.x == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[0])) : "memory");
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[1])) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    failed = 0;
-  }
-  __syncthreads();
-  auto issue = [&](int k) {  // thread 0: chunk k into buffer k & 1
-    const int4 ch = __ldg(chunks + c0 + k);
-    uint64_t *bar = &full[k & 1];
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(ch.w)
-                 : "memory");
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_addr(reinterpret_cast<char *>(sbuf) + (k & 1) * kBulkBytes)),
-        "l"(reinterpret_cast<const char *>(recs) + (uint64_t)(uint32_t)ch.z * 16u), "r"(ch.w), "r"(smem_addr(bar))
-        : "memory");
-  };
-  if (threadIdx.x == 0) {
-    if (nc > 0) issue(0);
-    if (nc > 1) issue(1);
-  }
-
-  float acc[KM][NB];
-#pragma unroll
-  for (int k = 0; k < KM; ++k)
-#pragma unroll
-    for (int q = 0; q < NB; ++q) acc[k][q] = 0.f;
-
-  int k = 0;
-  for (; k < nc; ++k) {
-    if (!bulk_wait(&full[k & 1], (k >> 1) & 1)) {
-      failed = 1;  // benign race: every writer stores 1
-    }
-    __syncthreads();
-    if (failed) break;
-    const int4 ch = __ldg(chunks + c0 + k);
-    // the chunk's records sit in buffer k & 1 from its first 16-byte unit
-    // ch.z on; item offsets count words (VT 0, 3) or halfwords (VT 1, 2)
-    const uint32_t *buf = sbuf + (k & 1) * (kBulkBytes / 4);
-    constexpr int kUnitsPer16 = (VT == 1 || VT == 2) ? 8 : 4;
-    const uint32_t first = (uint32_t)ch.z * kUnitsPer16;
-    for (int it = ch.x + warp; it < ch.y; it += nw) {
-      const int2 item = __ldg(items + it);
-      dispatch_narrow<KM, NB, VT, true>(item.y & 0xffff, buf, (uint32_t)item.x - first, item.y >> 16, B, ldb, lane,
-                                        acc);
-    }
-    __syncthreads();  // buffer k & 1 consumed
-    if (threadIdx.x == 0 && k + 2 < nc) issue(k + 2);
-  }
-  if (failed) {
-    // wait (bounded) for this CTA's copies still in flight, then leave C alone
-    if (threadIdx.x == 0) {
-      atomicExch(status, 6);
-      for (int j = k; j < nc && j < k + 2; ++j) bulk_wait(&full[j & 1], (j >> 1) & 1);
-    }
-    return;
-  }
-
-  float v[V];
-#pragma unroll
-  for (int i = 0; i < V; ++i) v[i] = (i < KM * NB) ? acc[i / NB][i % NB] : 0.f;
-  warp_transpose_reduce<V>(v, lane);
-  constexpr int kRep = 32 / V;
-  if ((lane % kRep) == 0) red[warp][transpose_reduce_index<V>(lane)] = v[0];
-  __syncthreads();
-  if (threadIdx.x < KM * NB) {
-    float sum = 0.f;
-    for (int w = 0; w < nw; ++w) sum += red[w][threadIdx.x];
-    const int kk = threadIdx.x / NB, q = threadIdx.x % NB;
-    const int64_t row = (int64_t)panel * KM + kk;
-    if (row < rows) {
-      float *c = C + row * ldc + q;
-      *c = accumulate ? *c + sum : sum;
-    }
-  }
-}
-
-using NarrowBulkFn = void (*)(const uint32_t *, const int2 *, const int4 *, const int32_t *, const int32_t *,
-                              const float *, int64_t, float *, int64_t, int64_t, int, int *);
-
 using WideFn = void (*)(WideArgs, const WideArgs *, const int32_t *, int);
 using NarrowFn = void (*)(const uint32_t *, const int2 *, const int32_t *, const int32_t *, const float *,
                           int64_t, float *, int64_t, int64_t, int);
@@ -972,9 +841,3 @@ sc::NarrowFn sc_narrow_kernel_km3(int nb, int vt);
 sc::NarrowFn sc_narrow_kernel_km4(int nb, int vt);
 sc::NarrowFn sc_narrow_kernel_km5(int nb, int vt);
 sc::NarrowFn sc_narrow_kernel_km6(int nb, int vt);
-sc::NarrowBulkFn sc_narrow_bulk_kernel_km1(int nb, int vt);
-sc::NarrowBulkFn sc_narrow_bulk_kernel_km2(int nb, int vt);
-sc::NarrowBulkFn sc_narrow_bulk_kernel_km3(int nb, int vt);
-sc::NarrowBulkFn sc_narrow_bulk_kernel_km4(int nb, int vt);
-sc::NarrowBulkFn sc_narrow_bulk_kernel_km5(int nb, int vt);
-sc::NarrowBulkFn sc_narrow_bulk_kernel_km6(int nb, int vt);

@@ -87,10 +87,6 @@ struct sc_plan {
   bool dense_bf16 = false;      // bf16 tiles (SC_PLAN_DENSE_BF16) instead of 3xTF32
   int value_type = 0;           // stored values: 0 fp32, 1 fp16, 2 bf16 (compact small-B records)
   int record_vt = 0;            // record layout the narrow kernel reads: value_type, or 3 = split blocks
-  // Bulk-staged small-B kernel: per local panel, chunks of whole items of at
-  // most sc::kBulkBytes {first item, end item, first 16-byte unit, bytes}.
-  const int4 *bulk_chunks = nullptr;
-  const int32_t *bulk_chunk_ptr = nullptr;
   uint32_t flags = 0;           // SC_PLAN_* given at creation
   ~sc_plan() {
     if (dev || stage_b || stage_c || a_tiles || chunk_order || side || khalf_items[0] || side2) {
@@ -155,27 +151,6 @@ WideFn wide_kernel_raw(int km, int vec, bool batch) {
   }
 }
 WideFn wide_kernel(int km, int vec, bool batch) { return with_carveout(wide_kernel_raw(km, vec, batch)); }
-
-sc::NarrowBulkFn narrow_bulk_kernel(int km, int nb, int vt) {
-  switch (km) {
-    case 1: return sc_narrow_bulk_kernel_km1(nb, vt);
-    case 2: return sc_narrow_bulk_kernel_km2(nb, vt);
-    case 3: return sc_narrow_bulk_kernel_km3(nb, vt);
-    case 4: return sc_narrow_bulk_kernel_km4(nb, vt);
-    case 5: return sc_narrow_bulk_kernel_km5(nb, vt);
-    default: return sc_narrow_bulk_kernel_km6(nb, vt);
-  }
-}
-
-// SC_NARROW_BULK=0 runs small-B plans on the per-lane-load kernel instead of
-// the bulk-staged one (measurement switch).
-bool narrow_bulk_enabled() {
-  static const bool v = [] {
-    const char *e = getenv("SC_NARROW_BULK");
-    return !(e && e[0] == '0');
-  }();
-  return v;
-}
 
 NarrowFn narrow_kernel(int km, int nb, int vt) {
   switch (km) {
@@ -605,44 +580,6 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
     std::vector<uint16_t>().swap(recs16);
   }
 
-  // Bulk chunks of small-B plans: consecutive items of a panel whose
-  // 16-byte-rounded record range fits sc::kBulkBytes.
-  std::vector<int4> bchunks;
-  std::vector<int32_t> bchunk_ptr;
-  if (n == 1 || n == 2 || n == 4) {
-    const int vt = plan->record_vt;
-    const uint64_t unit = (vt == 1 || vt == 2) ? 2 : 4;  // bytes per offset unit
-    auto item_end_bytes = [&](const int2 &it) {
-      const int len = it.y >> 16, P = __builtin_popcount(it.y & 0xffff);
-      uint64_t words;
-      if (vt == 3) {
-        words = sc::split_col_words(len) + sc::split_val_words(len, P);
-        return (uint64_t)it.x * 4 + words * 4;
-      }
-      return ((uint64_t)it.x + (uint64_t)len * sc::rec_stride(P)) * unit;
-    };
-    bchunk_ptr.push_back(0);
-    for (int64_t lp = 0; lp < plan->panels; ++lp) {
-      int32_t i = item_ptr[lp];
-      while (i < item_ptr[lp + 1]) {
-        const uint64_t b0 = ((uint64_t)items[i].x * unit) & ~(uint64_t)15;
-        int32_t j = i;
-        uint64_t b1 = b0;
-        while (j < item_ptr[lp + 1]) {
-          const uint64_t e = (item_end_bytes(items[j]) + 15) & ~(uint64_t)15;
-          if (j > i && e - b0 > (uint64_t)sc::kBulkBytes) break;
-          b1 = e;
-          ++j;
-        }
-        require(b1 - b0 <= (uint64_t)sc::kBulkBytes, SC_ERR_UNSUPPORTED, "internal: item larger than a bulk chunk");
-        require(b0 / 16 < (uint64_t)INT32_MAX, SC_ERR_UNSUPPORTED, "record stream too large for bulk chunks");
-        bchunks.push_back(make_int4(i, j, (int)(b0 / 16), (int)(b1 - b0)));
-        i = j;
-      }
-      bchunk_ptr.push_back((int32_t)bchunks.size());
-    }
-  }
-
   std::vector<int32_t> order(plan->panels);
   for (int64_t i = 0; i < plan->panels; ++i) order[i] = (int32_t)i;
   std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return work[a] > work[b]; });
@@ -682,9 +619,7 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   const size_t b_items = align(std::max<size_t>(1, items.size()) * sizeof(int2));
   const size_t b_ptr = align(item_ptr.size() * 4);
   const size_t b_order = align(std::max<size_t>(1, order.size()) * 4);
-  const size_t b_bchunks = bchunks.empty() ? 0 : align(bchunks.size() * sizeof(int4)) + align(bchunk_ptr.size() * 4);
-  const size_t b_status = plan->kernel == 1 ? 256 : 0;
-  plan->dev_bytes = b_recs + b_items + b_ptr + b_order + b_bchunks + b_status;
+  plan->dev_bytes = b_recs + b_items + b_ptr + b_order;
   cuda_check(cudaMalloc(&plan->dev, plan->dev_bytes), "cudaMalloc(plan)");
   char *base = static_cast<char *>(plan->dev);
   plan->recs = reinterpret_cast<const uint32_t *>(base);
@@ -701,23 +636,6 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
     cuda_check(cudaMemcpy(base + b_recs + b_items + b_ptr, order.data(), order.size() * 4,
                           cudaMemcpyHostToDevice),
                "upload panel order");
-  {
-    char *q = base + b_recs + b_items + b_ptr + b_order;
-    if (!bchunks.empty()) {
-      plan->bulk_chunks = reinterpret_cast<const int4 *>(q);
-      cuda_check(cudaMemcpy(q, bchunks.data(), bchunks.size() * sizeof(int4), cudaMemcpyHostToDevice),
-                 "upload bulk chunks");
-      q += align(bchunks.size() * sizeof(int4));
-      plan->bulk_chunk_ptr = reinterpret_cast<const int32_t *>(q);
-      cuda_check(cudaMemcpy(q, bchunk_ptr.data(), bchunk_ptr.size() * 4, cudaMemcpyHostToDevice),
-                 "upload bulk chunks");
-      q += align(bchunk_ptr.size() * 4);
-    }
-    if (b_status) {
-      plan->status = reinterpret_cast<int *>(q);
-      cuda_check(cudaMemset(q, 0, 4), "clear status");
-    }
-  }
   if (plan->kernel == 2 && plan->rows > 0 && use_dense(*plan, cf)) build_dense(*plan, cf, pb, rowbits);
   if (plan->kernel == 2 && plan->cols >= 4096 && plan->panels > 0) build_ksplit(*plan, recs, items, item_ptr);
   if (plan->kernel != 3 && plan->panels >= sc_plan::kHostChunks) {
@@ -785,12 +703,7 @@ void launch_panels(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ld
     return;
   }
   if (p->kernel == 1) {
-    if (p->bulk_chunks && narrow_bulk_enabled() && ldb % nb == 0 && aligned(B, 4 * nb)) {
-      sc::NarrowBulkFn fn = narrow_bulk_kernel((int)p->km, nb, p->record_vt);
-      fn<<<dim3((unsigned)count), 128, 2 * sc::kBulkBytes, stream>>>(p->recs, p->item_list, p->bulk_chunks,
-                                                                      p->bulk_chunk_ptr, order, B, ldb, C, ldc,
-                                                                      p->rows, accumulate, p->status);
-    } else if (ldb % nb == 0 && aligned(B, 4 * nb)) {
+    if (ldb % nb == 0 && aligned(B, 4 * nb)) {
       NarrowFn fn = narrow_kernel((int)p->km, nb, p->record_vt);
       fn<<<dim3((unsigned)count), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, order, B, ldb, C, ldc,
                                                          p->rows, accumulate);
