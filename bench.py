@@ -752,6 +752,13 @@ def main():
     fp32_peak = props.multi_processor_count * 128 * 2 * sm_max * 1e6 / 1e12
     local_flops = 2.0 * sum(j["nnz_local"] for j in jobs) * N
     traffic = measured_traffic(f"config{args.config}_n{N}_m{km}_{kn}_gpus{world}")
+    # L1/shared data-pipe bound of the gather kernel (wide-B plans): every
+    # (panel, column) entry loads one N-float B row (ceil(4N/128) wavefronts of
+    # 128 bytes) plus ~1 wavefront for its record; the pipe moves one wavefront
+    # per cycle per SM
+    wide_entries = sum(j["plan"].info["entries"] for j in jobs if j["plan"].info["kernel"] == 2)
+    gather_us = (wide_entries * (-(-4 * N // 128) + 1) / (props.multi_processor_count * sm_max * 1e6) * 1e6
+                 if wide_entries else None)
     info = jobs[0]["plan"].info
 
     line = {
@@ -786,7 +793,9 @@ def main():
                      "algorithmic_bytes": alg_bytes,
                      "fp32_tflops": local_flops / (kern_ms * 1e-3) / 1e12,
                      "fp32_peak_tflops": fp32_peak,
-                     "fp32_frac": local_flops / (kern_ms * 1e-3) / 1e12 / fp32_peak},
+                     "fp32_frac": local_flops / (kern_ms * 1e-3) / 1e12 / fp32_peak,
+                     "gather_bound_us": gather_us,
+                     "gather_frac": (gather_us / (kern_ms * 1e3)) if gather_us else None},
         "e2e": {"value": e2e_value, "unit": "GFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_s * 1e3},
         "gpu_launches": args.steps * (len(batches) if batches else len(jobs)) * (2 if peer_mode and use_flags else 1),

@@ -94,3 +94,45 @@ def test_gather_row_blocks_gloo(world):
         p.join(120)
         assert p.exitcode == 0
     assert all(result[r] for r in range(world))
+
+
+def _dead_rank_worker(rank, world, port, result):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    a, B = wl.config3((2048, 512), 16)
+    m = a[0]
+    cuts = pt.balanced_panel_cuts(a[2], m, 4, world)
+    if rank == 1:
+        os._exit(3)  # this rank dies between steps, before the exchange
+    r0, r1 = pt.panel_rows(cuts, rank, 4, m)
+    blk = pt.row_slice(a, r0, r1)
+    Cb = cpu.spmm_csr_float(blk[2], blk[3], blk[4], B)
+    try:
+        pt.gather_row_blocks(torch.from_numpy(Cb), cuts, rank, world, 4, m)
+        result[rank] = "completed"
+    except Exception as ex:  # the collective must fail, not hang
+        result[rank] = "raised: " + type(ex).__name__
+
+
+def test_dead_rank_is_detected_gloo():
+    """A rank that exits before the C exchange: the survivor's collective
+    ends with an error within the process-group timeout instead of hanging."""
+    import time
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    result = mgr.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_rank_worker, args=(r, 2, port, result)) for r in range(2)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(90)
+    assert all(p.exitcode is not None for p in procs), "a rank hung"
+    assert procs[1].exitcode == 3
+    assert result.get(0, "").startswith("raised"), result.get(0)
+    assert time.time() - t0 < 90
