@@ -38,6 +38,9 @@ extern "C" void *ref_gpu_spmm_create(const char *cfmtx_path, const float *hB, in
   cudaMemset(h->dY, 0, (size_t)h->rows * n_cols_b * sizeof(float));
   cudaMemcpy(h->dX, hB, (size_t)h->cols * n_cols_b * sizeof(float), cudaMemcpyHostToDevice);
   h->mf = allocateAndCopyMixedFormat(h->host);
+  // the upload's zero-byte copies (patterns without entries) leave a
+  // non-sticky error behind; clear it so that the launch check sees its own
+  cudaGetLastError();
   return cudaDeviceSynchronize() == cudaSuccess ? h : nullptr;
 }
 

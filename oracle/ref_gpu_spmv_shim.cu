@@ -34,6 +34,9 @@ extern "C" void *ref_gpu_spmv_create(const char *cfmtx_path, const float *hx) {
   cudaMemset(h->dY, 0, (size_t)h->rows * sizeof(float));
   cudaMemcpy(h->dX, hx, (size_t)h->cols * sizeof(float), cudaMemcpyHostToDevice);
   h->mf = allocateAndCopyMixedFormat(h->host);
+  // the upload's zero-byte copies (patterns without entries) leave a
+  // non-sticky error behind; clear it so that the launch check sees its own
+  cudaGetLastError();
   return cudaDeviceSynchronize() == cudaSuccess ? h : nullptr;
 }
 
