@@ -313,6 +313,43 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
   }
 }
 
+// Rows [kc*BK, kc*BK + BK) x columns [nt*128, nt*128 + 128) of B into T (zero
+// past K or N).  With 16-byte aligned rows every thread issues its BK/8
+// float4 loads together (the scalar form left this kernel latency-bound);
+// otherwise scalar loads.
+template <int BK>
+__device__ __forceinline__ void load_b_chunk(const DenseMat &m, int nt, int kc, float (&T)[BK][kBN + 1]) {
+  const bool vec = (reinterpret_cast<uintptr_t>(m.B) % 16 == 0) && (m.ldb % 4 == 0);
+  if (vec) {
+    constexpr int kQuads = BK * kBN / 4;
+    constexpr int kPer = kQuads / 256;  // launched with 256 threads
+    float4 x[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int q = threadIdx.x + i * 256;
+      const int k = q / (kBN / 4), n4 = (q % (kBN / 4)) * 4;
+      const int gk = kc * BK + k, gn = nt * kBN + n4;
+      x[i] = (gk < m.k_rows && gn < m.n_cols) ? __ldg(reinterpret_cast<const float4 *>(m.B + (int64_t)gk * m.ldb + gn))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int q = threadIdx.x + i * 256;
+      const int k = q / (kBN / 4), n4 = (q % (kBN / 4)) * 4;
+      T[k][n4] = x[i].x;
+      T[k][n4 + 1] = x[i].y;
+      T[k][n4 + 2] = x[i].z;
+      T[k][n4 + 3] = x[i].w;
+    }
+  } else {
+    for (int e = threadIdx.x; e < kBN * BK; e += blockDim.x) {
+      const int n = e % kBN, k = e / kBN;
+      const int gk = kc * BK + k, gn = nt * kBN + n;
+      T[k][n] = (gk < m.k_rows && gn < m.n_cols) ? __ldg(m.B + (int64_t)gk * m.ldb + gn) : 0.f;
+    }
+  }
+}
+
 // B (K x N row-major fp32) -> per (n tile, K chunk) [hi | lo] K-major
 // swizzled images; rows of a B image are C columns (n), K-chunk tail zeroed.
 // Block (x, y): tile x of matrix y.  The 32 x 128 chunk is read coalesced
@@ -326,11 +363,7 @@ __global__ void __launch_bounds__(256) split_b_kernel(DenseMat one, const DenseM
   const int tile = blockIdx.x;
   if (tile >= m.n_tiles * m.k_chunks) return;
   const int nt = tile / m.k_chunks, kc = tile % m.k_chunks;
-  for (int e = threadIdx.x; e < kBN * kBK; e += blockDim.x) {
-    const int n = e % kBN, k = e / kBN;
-    const int gk = kc * kBK + k, gn = nt * kBN + n;
-    T[k][n] = (gk < m.k_rows && gn < m.n_cols) ? __ldg(m.B + (int64_t)gk * m.ldb + gn) : 0.f;
-  }
+  load_b_chunk<kBK>(m, nt, kc, T);
   __syncthreads();
   float4 *hi = reinterpret_cast<float4 *>(m.b_tiles + ((size_t)nt * m.k_chunks + kc) * 2 * kTileBytes);
   float4 *lo = hi + kTileBytes / 16;
@@ -361,11 +394,7 @@ __global__ void __launch_bounds__(256) split_b_bf16_kernel(DenseMat one, const D
   const int tile = blockIdx.x;
   if (tile >= m.n_tiles * m.k_chunks) return;
   const int nt = tile / m.k_chunks, kc = tile % m.k_chunks;
-  for (int e = threadIdx.x; e < kBN * kBKb; e += blockDim.x) {
-    const int n = e % kBN, k = e / kBN;
-    const int gk = kc * kBKb + k, gn = nt * kBN + n;
-    T[k][n] = (gk < m.k_rows && gn < m.n_cols) ? __ldg(m.B + (int64_t)gk * m.ldb + gn) : 0.f;
-  }
+  load_b_chunk<kBKb>(m, nt, kc, T);
   __syncthreads();
   uint4 *img = reinterpret_cast<uint4 *>(m.b_tiles + ((size_t)nt * m.k_chunks + kc) * kTileBytes);
   // 16-byte chunk q: row n = q / 8, physical chunk c = q % 8 holding logical
