@@ -207,8 +207,7 @@ struct WideArgs {
 #ifndef SC_WIDE_BATCH_MINB
 #define SC_WIDE_BATCH_MINB 3
 #endif
-constexpr int kRecBufWords = kItemEntries * 8;  // one item block (4 + 4P <= 32 bytes an entry) and
-                                                // the reads of its last group
+constexpr int kRecBufWords = kItemEntries * 8;  // one item of the widest stride
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
   const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
@@ -217,58 +216,67 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
-// Item blocks of wide plans: [len 32-bit columns, 0-fill to 16 B][len * P
-// fp32 values, 0-fill to 16 B], 16-byte aligned -- 4 + 4P bytes per entry
-// (the interleaved record padded P = 4 to 32 bytes), and read back from
-// shared memory as 16-byte broadcasts: one wavefront covers four columns, or
-// four values.
-__host__ __device__ constexpr uint32_t wide_col_words(int len) { return (uint32_t)((len + 3) / 4) * 4u; }
-__host__ __device__ constexpr uint32_t wide_val_words(int len, int p) { return (uint32_t)((len * p + 3) / 4) * 4u; }
-
-// Warp-cooperative copy of an item's block (16-byte chunks) into `dst`.
+// Warp-cooperative copy of an item's records (16-byte chunks) into `dst`.
 __device__ __forceinline__ void copy_item_recs(uint32_t *dst, const uint32_t *__restrict__ recs, int2 item,
                                                int lane) {
   const int len = item.y >> 16;
   const int P = __popc(item.y & 0xffff);
-  const int chunks = (int)(wide_col_words(len) + wide_val_words(len, P)) >> 2;
+  const int S = P == 1 ? 2 : (P <= 3 ? 4 : 8);
+  const int chunks = (len * S + 3) >> 2;
   const uint4 *src = reinterpret_cast<const uint4 *>(recs + (uint32_t)item.x);
   for (int c = lane; c < chunks; c += 32) cp_async16(reinterpret_cast<uint4 *>(dst) + c, src + c);
 }
 
-// Columns and values of entries e0 .. e0+U-1 (U a multiple of 4, e0 a
-// multiple of U) of the item block staged at rbuf; values past len read as 0
-// (the words there belong to older items).
-template <int P, int U>
-__device__ __forceinline__ void lds_group(const uint32_t *rbuf, int len, int e0, uint32_t (&col)[U], float (&v)[U][P]) {
-  static_assert(U % 4 == 0, "groups of four entries");
+template <int P>
+__device__ __forceinline__ void lds_rec(const uint32_t *r, uint32_t &col, float (&v)[P]) {
+  constexpr int S = rec_stride(P);
+  if constexpr (S == 2) {
+    const uint2 t = *reinterpret_cast<const uint2 *>(r);
+    col = t.x; v[0] = __uint_as_float(t.y);
+  } else if constexpr (S == 4) {
+    const uint4 t = *reinterpret_cast<const uint4 *>(r);
+    col = t.x;
+    const uint32_t w[3] = {t.y, t.z, t.w};
 #pragma unroll
-  for (int i = 0; i < U / 4; ++i) {
-    const uint4 t = *reinterpret_cast<const uint4 *>(rbuf + e0 + 4 * i);
-    col[4 * i] = t.x; col[4 * i + 1] = t.y; col[4 * i + 2] = t.z; col[4 * i + 3] = t.w;
+    for (int p = 0; p < P; ++p) v[p] = __uint_as_float(w[p]);
+  } else {
+    const uint4 a = *reinterpret_cast<const uint4 *>(r);
+    const uint4 b = *(reinterpret_cast<const uint4 *>(r) + 1);
+    col = a.x;
+    const uint32_t w[7] = {a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int p = 0; p < P; ++p) v[p] = __uint_as_float(w[p]);
   }
-  const uint32_t *vals = rbuf + wide_col_words(len) + e0 * P;
-  uint32_t f[U * P];
-#pragma unroll
-  for (int i = 0; i < U * P / 4; ++i) {
-    const uint4 t = *reinterpret_cast<const uint4 *>(vals + 4 * i);
-    f[4 * i] = t.x; f[4 * i + 1] = t.y; f[4 * i + 2] = t.z; f[4 * i + 3] = t.w;
-  }
-#pragma unroll
-  for (int u = 0; u < U; ++u)
-#pragma unroll
-    for (int p = 0; p < P; ++p) v[u][p] = e0 + u < len ? __uint_as_float(f[u * P + p]) : 0.f;
 }
 
 template <int KM, int MASK, int VEC, int UW>
 __device__ __forceinline__ void seg_wide(const uint32_t *rbuf, int len, const char *__restrict__ Bcol,
                                          uint32_t ldb_bytes, bool active, float (&acc)[KM][VEC]) {
   constexpr int P = popc_c(MASK);
+  constexpr int S = rec_stride(P);
   constexpr int U = P <= 2 ? UW : 4;
   for (int e0 = 0; e0 < len; e0 += U) {
     float v[U][P];
     float b[U][VEC];
     uint32_t col[U];
-    lds_group<P, U>(rbuf, len, e0, col, v);
+    if constexpr (S == 2 && U % 2 == 0) {
+      // two 8-byte records per 16-byte broadcast load (one shared-memory
+      // wavefront instead of two); the pair index is clamped into the item,
+      // and a pair's second record past an odd length is the segment's zero
+      // fill (copied with the item's last 16-byte chunk)
+#pragma unroll
+      for (int u = 0; u < U; u += 2) {
+        const int e = min(e0 + u, (len - 1) & ~1);
+        const uint4 t = *reinterpret_cast<const uint4 *>(rbuf + e * 2);
+        col[u] = t.x;
+        v[u][0] = __uint_as_float(t.y);
+        col[u + 1] = t.z;
+        v[u + 1][0] = __uint_as_float(t.w);
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) lds_rec<P>(rbuf + min(e0 + u, len - 1) * S, col[u], v[u]);
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (active && e0 + u < len) {
@@ -313,6 +321,7 @@ __device__ __forceinline__ void add_rows(int mask, const float (&t)[P][W], float
 template <int KM, int P, int VEC, int UW>
 __device__ __forceinline__ void seg_wide_pc(const uint32_t *rbuf, int len, const char *__restrict__ Bcol,
                                             uint32_t ldb_bytes, bool active, int mask, float (&acc)[KM][VEC]) {
+  constexpr int S = rec_stride(P);
   constexpr int U = P <= 2 ? UW : 4;
   float t[P][VEC];
 #pragma unroll
@@ -322,12 +331,12 @@ __device__ __forceinline__ void seg_wide_pc(const uint32_t *rbuf, int len, const
   for (int e0 = 0; e0 < len; e0 += U) {
     float v[U][P];
     float b[U][VEC];
-    uint32_t col[U];
-    lds_group<P, U>(rbuf, len, e0, col, v);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
+      uint32_t col;
+      lds_rec<P>(rbuf + min(e0 + u, len - 1) * S, col, v[u]);
       if (active && e0 + u < len) {
-        load_b<VEC>(reinterpret_cast<const float *>(Bcol + (uint64_t)col[u] * ldb_bytes), b[u]);
+        load_b<VEC>(reinterpret_cast<const float *>(Bcol + (uint64_t)col * ldb_bytes), b[u]);
       } else {
 #pragma unroll
         for (int q = 0; q < VEC; ++q) b[u][q] = 0.f;

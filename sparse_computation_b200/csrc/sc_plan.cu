@@ -69,8 +69,7 @@ struct sc_plan {
   // below ksplit, half 1 the rest, so the host entry point can start on the
   // first rows of B while the second ones are still being copied.
   int64_t ksplit = 0;                         // 0: no split lists
-  int2 *khalf_items[2] = {nullptr, nullptr};  // one allocation (with the halves' records)
-  const uint32_t *khalf_recs = nullptr;
+  int2 *khalf_items[2] = {nullptr, nullptr};  // one allocation
   int32_t *khalf_ptr[2] = {nullptr, nullptr};
   cudaStream_t side2 = nullptr;
   cudaEvent_t host_ev[5] = {};
@@ -338,59 +337,48 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
 }
 
 // K-split item lists for the host entry point.  Each item's entries are
-// split at the first column >= ksplit, and each part gets its own item block
-// in a second record stream (the halves' blocks), so both parts keep the
-// 16-byte-aligned block layout.  Entries of an item must be in increasing
-// column order (the coarsener's merge order); otherwise no split lists are
-// built.
+// split at the first column >= ksplit; the cut is moved down to keep the
+// second part's records 16-byte aligned (the wide kernel stages records in
+// 16-byte pieces), which only moves a few low-column entries into half 1 --
+// half 1 runs after all of B has arrived, so that is still correct.  Entries
+// of an item must be in increasing column order (the coarsener's merge order);
+// otherwise no split lists are built.
 void build_ksplit(sc_plan &p, const std::vector<uint32_t> &recs, const std::vector<int2> &items,
                   const std::vector<int32_t> &item_ptr) {
   const int64_t kc = (p.cols / 2) & ~(int64_t)63;
   std::vector<int2> half[2];
   std::vector<int32_t> hptr[2];
-  std::vector<uint32_t> hrecs;  // the halves' own item blocks
   hptr[0].push_back(0);
   hptr[1].push_back(0);
-  auto emit = [&](int h, const int2 &item, int e0, int e1) {
-    const int mask = item.y & 0xffff, len = item.y >> 16, P = __builtin_popcount(mask), n = e1 - e0;
-    const size_t cols = (size_t)item.x, vals = cols + sc::wide_col_words(len);
-    const int64_t off = (int64_t)hrecs.size();
-    require(off < (int64_t)INT32_MAX, SC_ERR_UNSUPPORTED, "record stream exceeds 8 GiB");
-    hrecs.insert(hrecs.end(), recs.begin() + cols + e0, recs.begin() + cols + e1);
-    while (hrecs.size() % 4) hrecs.push_back(0);
-    hrecs.insert(hrecs.end(), recs.begin() + vals + (size_t)e0 * P, recs.begin() + vals + (size_t)e1 * P);
-    while (hrecs.size() % 4) hrecs.push_back(0);
-    half[h].push_back(make_int2((int)off, mask | (n << 16)));
-  };
   for (int64_t lp = 0; lp < p.panels; ++lp) {
     for (int32_t it = item_ptr[lp]; it < item_ptr[lp + 1]; ++it) {
       const int2 item = items[it];
-      const int len = item.y >> 16;
+      const int mask = item.y & 0xffff, len = item.y >> 16;
+      const int S = sc::rec_stride(__builtin_popcount(mask));
       int j = 0;
       int64_t prev = -1;
       for (int e = 0; e < len; ++e) {
-        const int64_t col = recs[(size_t)item.x + e];
+        const int64_t col = recs[(size_t)item.x + (size_t)e * S];
         if (col < prev) return;  // not column-sorted: no split lists
         prev = col;
         if (col < kc) j = e + 1;
       }
-      if (j > 0) emit(0, item, 0, j);
-      if (len - j > 0) emit(1, item, j, len);
+      const int step = S == 2 ? 2 : 1;  // 16-byte aligned start of the second part
+      const int j0 = j - j % step;
+      if (j0 > 0) half[0].push_back(make_int2(item.x, mask | (j0 << 16)));
+      if (len - j0 > 0) half[1].push_back(make_int2(item.x + j0 * S, mask | ((len - j0) << 16)));
     }
     hptr[0].push_back((int32_t)half[0].size());
     hptr[1].push_back((int32_t)half[1].size());
   }
-  if (hrecs.empty()) hrecs.assign(4, 0);
   auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
-  size_t off[5], tot = 0;
+  size_t off[4], tot = 0;
   for (int h = 0; h < 2; ++h) {
     off[2 * h] = tot;
     tot += al(std::max<size_t>(1, half[h].size()) * sizeof(int2));
     off[2 * h + 1] = tot;
     tot += al(hptr[h].size() * 4);
   }
-  off[4] = tot;
-  tot += al(hrecs.size() * 4);
   char *base = nullptr;
   cuda_check(cudaMalloc(&base, tot), "cudaMalloc(K-split items)");
   for (int h = 0; h < 2; ++h) {
@@ -402,9 +390,6 @@ void build_ksplit(sc_plan &p, const std::vector<uint32_t> &recs, const std::vect
     cuda_check(cudaMemcpy(p.khalf_ptr[h], hptr[h].data(), hptr[h].size() * 4, cudaMemcpyHostToDevice),
                "upload K-split items");
   }
-  p.khalf_recs = reinterpret_cast<const uint32_t *>(base + off[4]);
-  cuda_check(cudaMemcpy(base + off[4], hrecs.data(), hrecs.size() * 4, cudaMemcpyHostToDevice),
-             "upload K-split records");
   p.ksplit = kc;
   p.dev_bytes += tot;
 }
@@ -474,8 +459,6 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   // interleaved records (measurement switch).
   const bool split = !compact && (n == 1 || n == 2 || n == 4) && cf.num_cols <= 65536 && split_records_enabled();
   plan->record_vt = split ? 3 : plan->value_type;
-  // wide-B plans: item blocks of 32-bit columns then P fp32 values per entry
-  const bool wide_blocks = !(n == 1 || n == 2 || n == 4);
   if (compact) {
     require(n == 1 || n == 2 || n == 4, SC_ERR_UNSUPPORTED,
             "16-bit value records are for the small-B / SpMV kernel (n_cols_b 1, 2 or 4)");
@@ -505,19 +488,6 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
       int64_t seg_len = 0;
       std::vector<uint32_t> seg_cols, seg_vals;  // split mode: the segment's columns and value bits
       auto close_items = [&]() {
-        if (wide_blocks) {
-          for (int64_t e = 0; e < seg_len; e += item_cap) {
-            const int len = (int)std::min<int64_t>(item_cap, seg_len - e);
-            const int64_t off = (int64_t)recs.size();
-            require(off < (int64_t)INT32_MAX, SC_ERR_UNSUPPORTED, "record stream exceeds 8 GiB");
-            recs.insert(recs.end(), seg_cols.begin() + e, seg_cols.begin() + e + len);
-            while (recs.size() % 4) recs.push_back(0);
-            recs.insert(recs.end(), seg_vals.begin() + e * P, seg_vals.begin() + (e + len) * P);
-            while (recs.size() % 4) recs.push_back(0);
-            items.push_back(make_int2((int)off, rowbits[g] | (len << 16)));
-          }
-          return;
-        }
         if (split) {
           for (int64_t e = 0; e < seg_len; e += item_cap) {
             const int len = (int)std::min<int64_t>(item_cap, seg_len - e);
@@ -545,7 +515,7 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
         if (all_pad) continue;
         const int32_t col = pt.cb[j];
         require(col >= 0 && col < cf.num_cols, SC_ERR_FORMAT, "column index out of range in CF");
-        if (split || wide_blocks) {
+        if (split) {
           seg_cols.push_back((uint32_t)col);
           for (int p = 0; p < P; ++p) {
             const float v = pt.vals[(size_t)j * P + p];
@@ -778,7 +748,6 @@ void launch_khalf(sc_plan *p, int h, float *C, float *host_c, cudaStream_t strea
   while (vec > 1 && (p->n % vec != 0 || (host_c && !aligned(host_c, 4 * vec)))) vec >>= 1;
   const int slices = (int)((p->n + 32 * vec - 1) / (32 * vec));
   sc::WideArgs a = wide_args(p, p->stage_b, p->n, C, p->n);
-  a.recs = p->khalf_recs;
   a.items = p->khalf_items[h];
   a.item_ptr = p->khalf_ptr[h];
   if (host_c) {
