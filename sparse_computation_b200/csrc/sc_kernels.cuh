@@ -201,9 +201,6 @@ struct WideArgs {
 #ifndef SC_WIDE_MINB
 #define SC_WIDE_MINB 4
 #endif
-#ifndef SC_WIDE_SHFL
-#define SC_WIDE_SHFL 0
-#endif
 #ifndef SC_WIDE_BATCH_U
 #define SC_WIDE_BATCH_U 8
 #endif
@@ -262,20 +259,6 @@ __device__ __forceinline__ void seg_wide(const uint32_t *rbuf, int len, const ch
     float v[U][P];
     float b[U][VEC];
     uint32_t col[U];
-#if SC_WIDE_SHFL
-    if constexpr (S == 2 && U <= 16) {
-      // lane l < 2U reads word l of the group's records (one conflict-free
-      // 4-byte load), then each column / value is broadcast by a shuffle
-      const int lane = threadIdx.x & 31;
-      const int last = 2 * len - 1;
-      const uint32_t w = rbuf[min(2 * e0 + (lane & (2 * U - 1)), last)];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        col[u] = __shfl_sync(0xffffffffu, w, 2 * u);
-        v[u][0] = __uint_as_float(__shfl_sync(0xffffffffu, w, 2 * u + 1));
-      }
-    } else
-#endif
     if constexpr (S == 2 && U % 2 == 0) {
       // two 8-byte records per 16-byte broadcast load (one shared-memory
       // wavefront instead of two); the pair index is clamped into the item,
