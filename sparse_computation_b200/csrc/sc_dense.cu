@@ -133,14 +133,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // TMEM rows (C rows 32w..32w+31 of the tile) are owned by CTA w / (4/S); the
 // other CTAs send theirs into the owner's shared memory (slots of 32 rows x
 // 128 floats), then the owner adds them up and stores C.
-template <bool BATCH, bool BF16>
+template <bool BATCH, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *__restrict__ tasks, int accumulate,
                   int *status) {
   // tf32 x3: stage = A_hi, A_lo, B_hi, B_lo (64 KiB), 3 stages;
-  // bf16:    stage = A, B (32 KiB), 6 stages.
-  constexpr int NST = BF16 ? 6 : kStages;
-  constexpr int SB = BF16 ? 2 * kTileBytes : kStageBytes;
+  // bf16:    stage = A, B (32 KiB), 6 stages;
+  // bf16 x3: stage = A1, A2, A3, B1, B2, B3 (96 KiB), 2 stages.
+  constexpr bool BF16 = MODE != kModeTf32x3;
+  constexpr int NST = MODE == kModeBf16 ? 6 : (MODE == kModeBf16x3 ? 2 : kStages);
+  constexpr int SB = 2 * mode_images(MODE) * kTileBytes;
   extern __shared__ __align__(1024) uint8_t dsmem[];
   // 1024-byte aligned stage ring (the swizzle is applied on address bits).
   uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
@@ -183,7 +185,7 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
 
   if (threadIdx.x == 0 && nk > 0 && !m.starve) {
     // producer
-    constexpr int OP = BF16 ? kTileBytes : 2 * kTileBytes;  // bytes of one operand's images
+    constexpr int OP = mode_images(MODE) * kTileBytes;  // bytes of one operand's images
     for (int i = 0; i < nk; ++i) {
       const int s = i % NST;
       if (i >= NST && !mbar_wait(&empty_bar[s], ((i / NST) - 1) & 1, &abort_flag)) {
@@ -213,7 +215,25 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
       }
       tc_fence_after();
       const uint32_t base = smem_u32(ring + (size_t)s * SB);
-      if constexpr (BF16) {
+      if constexpr (MODE == kModeBf16x3) {
+        uint64_t a[3], b[3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          a[j] = sdesc(base + j * kTileBytes);
+          b[j] = sdesc(base + (3 + j) * kTileBytes);
+        }
+#pragma unroll
+        for (int k = 0; k < kBKb / 16; ++k) {
+          const uint64_t step = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
+          // smallest terms first; the first MMA of a tile starts the accumulator
+          mma_bf16(tmem, a[2] + step, b[0] + step, (i > 0 || k > 0) ? 1u : 0u);
+          mma_bf16(tmem, a[0] + step, b[2] + step, 1u);
+          mma_bf16(tmem, a[1] + step, b[1] + step, 1u);
+          mma_bf16(tmem, a[1] + step, b[0] + step, 1u);
+          mma_bf16(tmem, a[0] + step, b[1] + step, 1u);
+          mma_bf16(tmem, a[0] + step, b[0] + step, 1u);
+        }
+      } else if constexpr (BF16) {
         const uint64_t a = sdesc(base), b = sdesc(base + kTileBytes);
 #pragma unroll
         for (int k = 0; k < kBKb / 16; ++k) {
@@ -410,15 +430,48 @@ __global__ void __launch_bounds__(256) split_b_bf16_kernel(DenseMat one, const D
   }
 }
 
+// bf16 x3 mode: three images (x1, x2, x3 parts) per (n tile, 64-wide K chunk).
+template <bool BATCH>
+__global__ void __launch_bounds__(256) split_b_bf16x3_kernel(DenseMat one, const DenseMat *__restrict__ mats) {
+  __shared__ float T[kBKb][kBN + 1];
+  DenseMat m;
+  if constexpr (BATCH) m = mats[blockIdx.y];
+  else m = one;
+  const int tile = blockIdx.x;
+  if (tile >= m.n_tiles * m.k_chunks) return;
+  const int nt = tile / m.k_chunks, kc = tile % m.k_chunks;
+  load_b_chunk<kBKb>(m, nt, kc, T);
+  __syncthreads();
+  uint4 *img = reinterpret_cast<uint4 *>(m.b_tiles + ((size_t)nt * m.k_chunks + kc) * 3 * kTileBytes);
+  for (int q = threadIdx.x; q < kBN * 8; q += blockDim.x) {
+    const int n = q >> 3, c = q & 7;
+    const int k0 = (c ^ (n & 7)) << 3;
+    uint32_t w[3][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint16_t lo[3], hi[3];
+      bf16x3_split(T[k0 + 2 * j][n], lo);
+      bf16x3_split(T[k0 + 2 * j + 1][n], hi);
+#pragma unroll
+      for (int r = 0; r < 3; ++r) w[r][j] = (uint32_t)lo[r] | ((uint32_t)hi[r] << 16);
+    }
+#pragma unroll
+    for (int r = 0; r < 3; ++r) img[r * (kTileBytes / 16) + q] = make_uint4(w[r][0], w[r][1], w[r][2], w[r][3]);
+  }
+}
+
 }  // namespace
 }  // namespace dense
 }  // namespace sc
 
 int sc_dense_split_b(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, int nmats, int max_tiles,
-                     bool bf16, cudaStream_t s) {
+                     int mode, cudaStream_t s) {
   using namespace sc::dense;
   if (nmats <= 0 || max_tiles <= 0) return 0;
-  if (bf16) {
+  if (mode == kModeBf16x3) {
+    if (mats) split_b_bf16x3_kernel<true><<<dim3(max_tiles, nmats), 256, 0, s>>>(one, mats);
+    else split_b_bf16x3_kernel<false><<<dim3(max_tiles, 1), 256, 0, s>>>(one, nullptr);
+  } else if (mode == kModeBf16) {
     if (mats) split_b_bf16_kernel<true><<<dim3(max_tiles, nmats), 256, 0, s>>>(one, mats);
     else split_b_bf16_kernel<false><<<dim3(max_tiles, 1), 256, 0, s>>>(one, nullptr);
   } else {
@@ -429,18 +482,23 @@ int sc_dense_split_b(const sc::dense::DenseMat &one, const sc::dense::DenseMat *
 }
 
 int sc_dense_gemm(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, const int4 *tasks,
-                  int64_t ntasks, int split, bool bf16, int accumulate, int *status, cudaStream_t s) {
+                  int64_t ntasks, int split, int mode, int accumulate, int *status, cudaStream_t s) {
   using namespace sc::dense;
   if (ntasks <= 0) return 0;
-  const size_t smem = (size_t)kStages * kStageBytes + 1024;
-  auto fn = mats ? (bf16 ? dense_gemm_kernel<true, true> : dense_gemm_kernel<true, false>)
-                 : (bf16 ? dense_gemm_kernel<false, true> : dense_gemm_kernel<false, false>);
+  if (mode < 0 || mode > 2) return (int)cudaErrorInvalidValue;
+  const size_t smem = (size_t)kStages * kStageBytes + 1024;  // 192 KiB ring in every mode
+  using Fn = void (*)(DenseMat, const DenseMat *, const int4 *, int, int *);
+  const Fn table[2][3] = {{dense_gemm_kernel<false, kModeTf32x3>, dense_gemm_kernel<false, kModeBf16>,
+                           dense_gemm_kernel<false, kModeBf16x3>},
+                          {dense_gemm_kernel<true, kModeTf32x3>, dense_gemm_kernel<true, kModeBf16>,
+                           dense_gemm_kernel<true, kModeBf16x3>}};
+  const Fn fn = table[mats ? 1 : 0][mode];
   // one bit per device ordinal (< 32); concurrent callers may both set the
   // attribute, which is harmless, and the bit update is atomic
-  static std::atomic<unsigned> attr_done[4];
+  static std::atomic<unsigned> attr_done[6];
   int dev = 0;
   cudaGetDevice(&dev);
-  std::atomic<unsigned> &bits = attr_done[(mats ? 1 : 0) + (bf16 ? 2 : 0)];
+  std::atomic<unsigned> &bits = attr_done[(mats ? 1 : 0) + 2 * mode];
   if (dev >= 32 || !(bits.load() & (1u << dev))) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;

@@ -61,6 +61,19 @@ __host__ __device__ inline float tf32_round(float x) {
 // its swizzle and the per-k-step descriptor advance (32 bytes) are the same.
 constexpr int kBKb = 64;  // bf16 K per stage
 
+// 3xBF16 mode (the default for fp32 plans where it measures faster): every
+// fp32 operand split into three bf16 parts, x = x1 + x2 + x3 (x1 = rn(x),
+// x2 = rn(x - x1), x3 = rn(x - x1 - x2): 24 significant bits), and the
+// products x1y1 + x1y2 + x2y1 + x2y2 + x1y3 + x3y1 accumulated in fp32; the
+// dropped terms are ~2^-24 relative, inside the fp32 parity bound.  Six
+// images of 2 bytes instead of two of 4 bytes per element at the same
+// tensor-pipe time (kind::f16 runs at twice the kind::tf32 rate).
+constexpr int kModeTf32x3 = 0;
+constexpr int kModeBf16 = 1;
+constexpr int kModeBf16x3 = 2;
+__host__ __device__ constexpr int mode_images(int mode) { return mode == kModeBf16 ? 1 : (mode == kModeBf16x3 ? 3 : 2); }
+__host__ __device__ constexpr int mode_bk(int mode) { return mode == kModeTf32x3 ? kBK : kBKb; }
+
 __host__ __device__ inline uint32_t swz_offset_bf16(int r, int k) {
   const uint32_t chunk = (uint32_t)(k >> 3) ^ (uint32_t)(r & 7);
   return (uint32_t)r * 128u + chunk * 16u + (uint32_t)(k & 7) * 2u;
@@ -72,6 +85,25 @@ __host__ __device__ inline uint16_t bf16_bits(float x) {
   if ((u & 0x7f800000u) == 0x7f800000u) return (uint16_t)((u >> 16) | ((u & 0xffffu) ? 0x40u : 0u));  // inf/nan
   u += 0x7fffu + ((u >> 16) & 1u);
   return (uint16_t)(u >> 16);
+}
+
+__host__ __device__ inline float bf16_float(uint16_t h) {
+  const uint32_t u = (uint32_t)h << 16;
+  float y;
+  memcpy(&y, &u, 4);
+  return y;
+}
+
+// The three bf16 parts of x (3xBF16 mode).
+__host__ __device__ inline void bf16x3_split(float x, uint16_t (&h)[3]) {
+  h[0] = bf16_bits(x);
+  if ((h[0] & 0x7f80u) == 0x7f80u) {  // inf / nan (or rounded up to inf): no tail parts
+    h[1] = h[2] = 0;
+    return;
+  }
+  const float r1 = x - bf16_float(h[0]);
+  h[1] = bf16_bits(r1);
+  h[2] = bf16_bits(r1 - bf16_float(h[1]));
 }
 
 // One matrix of the dense path.
@@ -89,7 +121,7 @@ struct DenseMat {
   int n_cols;               // N (multiple of 128)
   int k_chunks;             // ceil(K / 32), or ceil(K / 64) in bf16 mode
   int n_tiles;              // N / 128
-  int bf16;                 // 1: bf16 tiles (one image per operand)
+  int bf16;                 // tile mode: kModeTf32x3, kModeBf16 or kModeBf16x3
   int starve = 0;           // test hook: the producer issues no copies, so the
                             // MMA issuer's bounded wait expires (status 2, then 3)
 };
@@ -100,7 +132,8 @@ struct DenseMat {
 // Launch helpers (sc_dense.cu).  `mats` is a device array of `nmats`
 // matrices (or nullptr with `one` used instead when nmats == 1); `tasks`
 // holds int4 {matrix, row block, n tile, kept chunks}, heaviest first.
+// `mode`: sc::dense::kModeTf32x3, kModeBf16 or kModeBf16x3.
 int sc_dense_split_b(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, int nmats, int max_tiles,
-                     bool bf16, cudaStream_t s);
+                     int mode, cudaStream_t s);
 int sc_dense_gemm(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, const int4 *tasks,
-                  int64_t ntasks, int split, bool bf16, int accumulate, int *status, cudaStream_t s);
+                  int64_t ntasks, int split, int mode, int accumulate, int *status, cudaStream_t s);

@@ -155,13 +155,13 @@ extern "C" int sc_spmm_dense_noalloc(const float *dA, int64_t lda, int64_t m, in
       reinterpret_cast<int4 *>(base + o_tasks), reinterpret_cast<int *>(base + o_status));
   noalloc_split_a<<<dim3((unsigned)kcs, (unsigned)rbs), 256, 0, s>>>(dA, lda, m, k, (int)kcs, base + o_a);
   cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess) e = (cudaError_t)sc_dense_split_b(mat, nullptr, 1, (int)(nts * kcs), false, s);
+  if (e == cudaSuccess) e = (cudaError_t)sc_dense_split_b(mat, nullptr, 1, (int)(nts * kcs), sc::dense::kModeTf32x3, s);
   // split K over a cluster when the tiles are too few to fill the GPU
   int split = 1;
   while (split < kMaxSplit && rbs * nts * split < 148 && kcs / (split * 2) >= 4) split <<= 1;
   if (e == cudaSuccess)
     e = (cudaError_t)sc_dense_gemm(mat, nullptr, reinterpret_cast<const int4 *>(base + o_tasks), rbs * nts, split,
-                                   false, accumulate, reinterpret_cast<int *>(base + o_status), s);
+                                   sc::dense::kModeTf32x3, accumulate, reinterpret_cast<int *>(base + o_status), s);
   if (e != cudaSuccess) {
     sc_set_error(std::string("sc_spmm_dense_noalloc: launch: ") + cudaGetErrorString(e));
     return SC_ERR_CUDA;

@@ -19,6 +19,10 @@
 #include "sc_dense.cuh"
 #include "sc_kernels.cuh"
 
+#ifndef SC_DEFAULT_DENSE_MODE
+#define SC_DEFAULT_DENSE_MODE 0
+#endif
+
 namespace {
 
 void require(bool cond, int code, const std::string &msg) {
@@ -84,7 +88,8 @@ struct sc_plan {
   int4 *dense_tasks = nullptr;  // {0, row block, n tile, kept chunks}, heaviest first
   int64_t dense_ntasks = 0;
   int dense_split = 1;          // CTAs (cluster) per task
-  bool dense_bf16 = false;      // bf16 tiles (SC_PLAN_DENSE_BF16) instead of 3xTF32
+  bool dense_bf16 = false;      // bf16 tiles (SC_PLAN_DENSE_BF16) instead of the fp32-exact splits
+  int dense_mode = 0;           // sc::dense::kModeTf32x3 / kModeBf16 / kModeBf16x3
   int value_type = 0;           // stored values: 0 fp32, 1 fp16, 2 bf16 (compact small-B records)
   int record_vt = 0;            // record layout the narrow kernel reads: value_type, or 3 = split blocks
   uint32_t flags = 0;           // SC_PLAN_* given at creation
@@ -220,12 +225,24 @@ sc::dense::DenseMat dense_mat(const sc_plan *p, const float *B, int64_t ldb, flo
   m.rows = p->rows;
   m.k_rows = (int)p->cols;
   m.n_cols = (int)p->n;
-  const int bk = p->dense_bf16 ? sc::dense::kBKb : sc::dense::kBK;
+  const int bk = sc::dense::mode_bk(p->dense_mode);
   m.k_chunks = (int)((p->cols + bk - 1) / bk);
   m.n_tiles = (int)(p->n / sc::dense::kBN);
-  m.bf16 = p->dense_bf16 ? 1 : 0;
+  m.bf16 = p->dense_mode;
   m.starve = (p->flags & SC_PLAN_TEST_STARVE) ? 1 : 0;
   return m;
+}
+
+// Exact-fp32 tile mode of dense plans: SC_DENSE_MODE=0 3xTF32, =2 3xBF16
+// (measurement switch; the default is the one measured faster).
+int default_dense_mode() {
+  static const int v = [] {
+    const char *e = getenv("SC_DENSE_MODE");
+    if (e && e[0] == '0') return sc::dense::kModeTf32x3;
+    if (e && e[0] == '2') return sc::dense::kModeBf16x3;
+    return SC_DEFAULT_DENSE_MODE;
+  }();
+  return v;
 }
 
 bool use_dense(const sc_plan &p, const sc_cf &cf) {
@@ -245,9 +262,9 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
   const int km = (int)p.km;
   const int64_t rows = p.rows, K = p.cols;
   const int64_t rbs = (rows + kBM - 1) / kBM;
-  const bool bf = p.dense_bf16;
-  const int bk = bf ? kBKb : kBK;            // K per chunk (one 128-byte tile row)
-  const int images = bf ? 1 : 2;            // bf16: one image; tf32: head + tail
+  const int mode = p.dense_mode;
+  const int bk = mode_bk(mode);             // K per chunk (one 128-byte tile row)
+  const int images = mode_images(mode);     // tf32: head + tail; bf16: one; bf16 x3: three parts
   const int kcs = (int)((K + bk - 1) / bk);
   // densify this plan's rows
   std::vector<float> A((size_t)rbs * kBM * K, 0.f);
@@ -288,7 +305,11 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
         for (int k = 0; k < bk; ++k) {
           const int64_t gk = (int64_t)kc * bk + k;
           const float x = gk < K ? A[(size_t)(b * kBM + r) * K + gk] : 0.f;
-          if (bf) {
+          if (mode == kModeBf16x3) {
+            uint16_t h[3];
+            bf16x3_split(x, h);
+            for (int j = 0; j < 3; ++j) memcpy(&tiles[off + j * kTileBytes + swz_offset_bf16(r, k)], &h[j], 2);
+          } else if (mode == kModeBf16) {
             const uint16_t h = bf16_bits(x);
             memcpy(&tiles[off + swz_offset_bf16(r, k)], &h, 2);
           } else {
@@ -452,6 +473,7 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   plan->device = device;
   plan->flags = flags;
   plan->dense_bf16 = (flags & SC_PLAN_DENSE_BF16) != 0;
+  plan->dense_mode = plan->dense_bf16 ? sc::dense::kModeBf16 : default_dense_mode();
   plan->value_type = (flags & SC_PLAN_VALUES_F16) ? 1 : ((flags & SC_PLAN_VALUES_BF16) ? 2 : 0);
   const bool compact = plan->value_type != 0;
   // fp32 small-B plans with K <= 65536: split item blocks (16-bit columns,
@@ -695,9 +717,9 @@ void launch_panels(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ld
   const int nb = (int)p->n;
   if (p->kernel == 3 && ldc % 4 == 0 && aligned(C, 16)) {
     const sc::dense::DenseMat m = dense_mat(p, B, ldb, C, ldc);
-    int e = sc_dense_split_b(m, nullptr, 1, m.n_tiles * m.k_chunks, p->dense_bf16, stream);
+    int e = sc_dense_split_b(m, nullptr, 1, m.n_tiles * m.k_chunks, p->dense_mode, stream);
     cuda_check((cudaError_t)e, "B tile split launch");
-    e = sc_dense_gemm(m, nullptr, p->dense_tasks, p->dense_ntasks, p->dense_split, p->dense_bf16, accumulate,
+    e = sc_dense_gemm(m, nullptr, p->dense_tasks, p->dense_ntasks, p->dense_split, p->dense_mode, accumulate,
                       p->status, stream);
     cuda_check((cudaError_t)e, "dense tile kernel launch");
     return;
@@ -1057,7 +1079,7 @@ struct sc_batch {
   int64_t tasks = 0;                     // wide group: (matrix, panel) tasks
   int64_t dense_ntasks = 0;
   int dense_split = 1, dense_max_tiles = 0;
-  bool dense_bf16 = false;  // all dense plans of a batch share one precision
+  int dense_mode = 0;  // all dense plans of a batch share one tile mode
   void *dev = nullptr;  // wide descs | wide order | dense mats | dense tasks | status
   sc::WideArgs *descs = nullptr;
   int2 *order = nullptr;
@@ -1094,8 +1116,8 @@ int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out) {
     require(p->device == b->device && p->n == b->n, SC_ERR_UNSUPPORTED,
             "plans of a batch must share device and n_cols_b");
     if (p->kernel == 3) {
-      if (b->dense_ids.empty()) b->dense_bf16 = p->dense_bf16;
-      require(p->dense_bf16 == b->dense_bf16, SC_ERR_UNSUPPORTED,
+      if (b->dense_ids.empty()) b->dense_mode = p->dense_mode;
+      require(p->dense_mode == b->dense_mode, SC_ERR_UNSUPPORTED,
               "dense-tile plans of a batch must share one precision (all bf16 or all 3xTF32)");
     }
     b->plans.push_back(plans[i]);
@@ -1133,7 +1155,7 @@ int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out) {
   for (size_t gi = 0; gi < b->dense_ids.size(); ++gi) {
     const sc_plan *p = plans[b->dense_ids[gi]];
     const int nts = (int)(p->n / sc::dense::kBN);
-    const int bk = p->dense_bf16 ? sc::dense::kBKb : sc::dense::kBK;
+    const int bk = sc::dense::mode_bk(p->dense_mode);
     const int kcs = (int)((p->cols + bk - 1) / bk);
     b->dense_max_tiles = std::max(b->dense_max_tiles, nts * kcs);
     std::vector<int32_t> rbp(p->row_blocks + 1);
@@ -1222,9 +1244,9 @@ int sc_batch_spmm(sc_batch *b, int32_t accumulate, void *stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (b->dense_ntasks > 0) {
     sc::dense::DenseMat none{};
-    int e = sc_dense_split_b(none, b->dmats, (int)b->dense_ids.size(), b->dense_max_tiles, b->dense_bf16, s);
+    int e = sc_dense_split_b(none, b->dmats, (int)b->dense_ids.size(), b->dense_max_tiles, b->dense_mode, s);
     cuda_check((cudaError_t)e, "B tile split launch");
-    e = sc_dense_gemm(none, b->dmats, b->dtasks, b->dense_ntasks, b->dense_split, b->dense_bf16, accumulate,
+    e = sc_dense_gemm(none, b->dmats, b->dtasks, b->dense_ntasks, b->dense_split, b->dense_mode, accumulate,
                       b->status, s);
     cuda_check((cudaError_t)e, "dense tile kernel launch");
   }
