@@ -152,7 +152,10 @@ int sc_plan_create_panels(const sc_cf *cf, int32_t n_cols_b, int32_t device,
 /* Test hook for the error path, not for production: in a dense-tile plan's
  * kernel the producer issues no copies, so the MMA issuer's bounded wait
  * expires with nothing in flight; every product of the plan then leaves C
- * unwritten and sets status 2/3 (sc_plan_status, SC_ERR_DEVICE). */
+ * unwritten and sets status 2/3 (sc_plan_status, SC_ERR_DEVICE).  In a
+ * small-B plan whose B is staged in shared memory (SpMV of a large
+ * matrix) the record copies are not issued: the bounded waits expire,
+ * C is left unwritten and the status is 7. */
 #define SC_PLAN_TEST_STARVE (1u << 30)
 int sc_plan_create_ex(const sc_cf *cf, int32_t n_cols_b, int32_t device, int64_t panel_begin,
                       int64_t panel_end, uint32_t flags, sc_plan **out);

@@ -48,7 +48,7 @@ SC_PLAN_DENSE_ON = 2
 SC_PLAN_DENSE_BF16 = 4
 SC_PLAN_VALUES_F16 = 8
 SC_PLAN_VALUES_BF16 = 16
-SC_PLAN_TEST_STARVE = 1 << 30  # test hook: dense-tile waits expire (error path tests)
+SC_PLAN_TEST_STARVE = 1 << 30  # test hook: dense-tile and staged small-B waits expire (error path tests)
 
 # Every symbol include/sc_b200.h declares (checked by the CPU tests).
 EXPORTED_SYMBOLS = (

@@ -31,20 +31,34 @@ sc::WideFn SC_CAT(sc_wide_kernel_km, SC_KM)(int vec, bool batch) {
 #else
 template <int VT>
 static sc::NarrowFn narrow_of(int nb) {
-  switch (nb) {
-    case 1: return sc::spmm_narrow_kernel<SC_KM, 1, VT>;
-    case 2: return sc::spmm_narrow_kernel<SC_KM, 2, VT>;
-    default: return sc::spmm_narrow_kernel<SC_KM, 4, VT>;
+  if constexpr (VT == 4) {
+    switch (nb) {
+      case 1: return sc::spmm_lane_kernel<SC_KM, 1>;
+      case 2: return sc::spmm_lane_kernel<SC_KM, 2>;
+      default: return sc::spmm_lane_kernel<SC_KM, 4>;
+    }
+  } else {
+    switch (nb) {
+      case 1: return sc::spmm_narrow_kernel<SC_KM, 1, VT>;
+      case 2: return sc::spmm_narrow_kernel<SC_KM, 2, VT>;
+      default: return sc::spmm_narrow_kernel<SC_KM, 4, VT>;
+    }
   }
 }
 
+sc::LaneXFn SC_CAT(sc_lane_x_kernel_km, SC_KM)(int nb) {
+  (void)nb;  // SpMV only (N = 2 staged measured no faster than split blocks)
+  return sc::spmm_lane_x_kernel<SC_KM, 1>;
+}
+
 // vt: 0 = fp32 records, 1 = fp16 compact records, 2 = bf16 compact records,
-// 3 = split blocks (16-bit columns, fp32 values)
+// 3 = split blocks (16-bit columns, fp32 values), 4 = lane blocks
 sc::NarrowFn SC_CAT(sc_narrow_kernel_km, SC_KM)(int nb, int vt) {
   switch (vt) {
     case 1: return narrow_of<1>(nb);
     case 2: return narrow_of<2>(nb);
     case 3: return narrow_of<3>(nb);
+    case 4: return narrow_of<4>(nb);
     default: return narrow_of<0>(nb);
   }
 }

@@ -822,6 +822,427 @@ spmm_narrow_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ i
   }
 }
 
+// ------------------------------------------------ narrow B, lane blocks ----
+// Lane blocks (the layout of fp32 SpMV plans whose vector fits in shared
+// memory).  A lane block holds U = kLaneSlots / P consecutive entries of one
+// pattern (mask) of a row panel: U 16-bit columns and U*P fp32 values.  The
+// blocks of one (panel, popcount) group are cut into items of up to 32
+// blocks, one per lane, stored chunk-major (the k-th 16-byte chunk of every
+// lane together, so that a warp-wide 16-byte load reads 512 contiguous bytes
+// from global memory or conflict-free from shared memory):
+//   [32 bytes: the mask of each block (uint8), zero-filled]
+//   [column region: 16-byte column chunks chunk-major, or one 8-byte chunk
+//    per lane when a block has at most 4 columns; padded to 16 bytes]
+//   [kLaneSlots/4 value chunks x nl x 16 bytes: 4 values each, entry-major]
+// with nl the blocks of the item; item header {word offset, P | nl << 8}.
+// Fill entries have column 0 and value 0.  A lane's loads do not depend on
+// P, so they can be issued before the item's pattern is dispatched.
+#ifndef SC_LANE_SLOTS
+#define SC_LANE_SLOTS 16
+#endif
+constexpr int kLaneSlots = SC_LANE_SLOTS;  // fp32 values per lane block (8 or 16)
+__host__ __device__ constexpr int lane_entries(int p) { return kLaneSlots / p; }
+// bytes of a lane's columns: 8, 16 or 32 (U <= 4, 8 or 16 columns)
+__host__ __device__ constexpr int lane_col_bytes(int p) {
+  return lane_entries(p) <= 4 ? 8 : (lane_entries(p) <= 8 ? 16 : 32);
+}
+__host__ __device__ constexpr uint32_t lane_col_region(int nl, int p) {
+  return ((uint32_t)nl * (uint32_t)lane_col_bytes(p) + 15u) & ~15u;
+}
+__host__ __device__ constexpr uint32_t lane_item_words(int nl, int p) {
+  return 8u + (lane_col_region(nl, p) + (uint32_t)nl * kLaneSlots * 4u) / 4u;
+}
+// Word of column u of lane l in an item's column region.
+__host__ __device__ constexpr uint32_t lane_col_word(int nl, int p, int l, int u) {
+  return lane_col_bytes(p) == 8 ? (uint32_t)(l * 2 + u / 2) : (uint32_t)(((u / 8) * nl + l) * 4 + (u % 8) / 2);
+}
+
+struct LaneBuf {
+  uint32_t m;                  // block mask (0: no block for this lane)
+  uint32_t c[kLaneSlots / 2];  // packed 16-bit columns
+  float v[kLaneSlots];
+};
+
+// Chunk c of lane `lane` of an item with nl blocks, from a region base.
+__device__ __forceinline__ const uint4 *lane_chunk(const char *region, int nl, int c, int lane) {
+  return reinterpret_cast<const uint4 *>(region) + (c * nl + lane);
+}
+
+template <bool SM>
+__device__ __forceinline__ void lane_load(const char *base, int2 item, int lane, LaneBuf &b) {
+  const int P = item.y & 0xff, nl = item.y >> 8;
+  if (lane < nl) {
+    b.m = ldro<SM>(reinterpret_cast<const uint8_t *>(base) + lane);
+    const int cb = P == 1 ? lane_col_bytes(1)
+                   : P == 2 ? lane_col_bytes(2)
+                   : P == 3 ? lane_col_bytes(3)
+                   : P == 4 ? lane_col_bytes(4)
+                   : P == 5 ? lane_col_bytes(5)
+                            : lane_col_bytes(6);
+    if (cb == 8) {
+      const uint2 c0 = ldro<SM>(reinterpret_cast<const uint2 *>(base + 32) + lane);
+      b.c[0] = c0.x; b.c[1] = c0.y;
+    } else {
+#pragma unroll
+      for (int i = 0; i < kLaneSlots / 8; ++i) {
+        if (i * 16 < cb) {
+          const uint4 c0 = ldro<SM>(lane_chunk(base + 32, nl, i, lane));
+          b.c[4 * i] = c0.x; b.c[4 * i + 1] = c0.y; b.c[4 * i + 2] = c0.z; b.c[4 * i + 3] = c0.w;
+        }
+      }
+    }
+    const char *vals = base + 32 + lane_col_region(nl, P);
+#pragma unroll
+    for (int i = 0; i < kLaneSlots / 4; ++i) {
+      const uint4 f = ldro<SM>(lane_chunk(vals, nl, i, lane));
+      b.v[4 * i] = __uint_as_float(f.x); b.v[4 * i + 1] = __uint_as_float(f.y);
+      b.v[4 * i + 2] = __uint_as_float(f.z); b.v[4 * i + 3] = __uint_as_float(f.w);
+    }
+  } else {
+    // no block: mask 0 adds nothing; columns 0 keep the gathers in range
+    b.m = 0;
+#pragma unroll
+    for (int i = 0; i < kLaneSlots / 2; ++i) b.c[i] = 0;
+#pragma unroll
+    for (int i = 0; i < kLaneSlots; ++i) b.v[i] = 0.f;
+  }
+}
+
+// One lane block against B in global memory (L1 gathers).
+template <int KM, int P, int NB>
+__device__ __forceinline__ void lane_compute(const LaneBuf &b, const float *__restrict__ B, int64_t ldb,
+                                             float (&acc)[KM][NB]) {
+  constexpr int U = lane_entries(P);
+  constexpr int G = NB == 4 ? 4 : (NB == 2 ? 8 : 16);  // B rows in flight per group
+  float t[P][NB];
+#pragma unroll
+  for (int p = 0; p < P; ++p)
+#pragma unroll
+    for (int q = 0; q < NB; ++q) t[p][q] = 0.f;
+#pragma unroll
+  for (int u0 = 0; u0 < U; u0 += G) {
+    float x[G][NB];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int u = u0 + g;
+      if (u < U) {
+        const uint32_t c = (b.c[u >> 1] >> ((u & 1) * 16)) & 0xffffu;
+        load_vec<NB>(B + (int64_t)c * ldb, x[g]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int u = u0 + g;
+      if (u < U) {
+#pragma unroll
+        for (int p = 0; p < P; ++p)
+#pragma unroll
+          for (int q = 0; q < NB; ++q) t[p][q] = fmaf(b.v[u * P + p], x[g][q], t[p][q]);
+      }
+    }
+  }
+  add_rows<KM, P, NB>((int)b.m, t, acc);
+}
+
+template <int KM, int NB, int LO, int HI>
+__device__ __forceinline__ void dispatch_lane(int P, const LaneBuf &b, const float *__restrict__ B, int64_t ldb,
+                                              float (&acc)[KM][NB]) {
+  if constexpr (HI - LO == 1) {
+    lane_compute<KM, LO, NB>(b, B, ldb, acc);
+  } else {
+    constexpr int MID = (LO + HI) / 2;
+    if (P < MID) dispatch_lane<KM, NB, LO, MID>(P, b, B, ldb, acc);
+    else dispatch_lane<KM, NB, MID, HI>(P, b, B, ldb, acc);
+  }
+}
+
+// Lane blocks with B read through L1 (N = 4, or a layout forced by
+// SC_NARROW_LAYOUT=lane): same arguments, grid and result as
+// spmm_narrow_kernel; each warp loads its next item before it gathers the B
+// rows of the current one.
+template <int KM, int NB>
+__global__ void __launch_bounds__(256)
+spmm_lane_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ items,
+                 const int32_t *__restrict__ item_ptr, const int32_t *__restrict__ order,
+                 const float *__restrict__ B, int64_t ldb, float *__restrict__ C, int64_t ldc,
+                 int64_t rows, int accumulate) {
+  constexpr int V = pow2_ceil(KM * NB);
+  static_assert(V <= 32, "KM*NB must not exceed 32");
+  __shared__ float red[8][V];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const int panel = order[blockIdx.x];
+
+  float acc[KM][NB];
+#pragma unroll
+  for (int k = 0; k < KM; ++k)
+#pragma unroll
+    for (int q = 0; q < NB; ++q) acc[k][q] = 0.f;
+
+  const int it0 = item_ptr[panel], it1 = item_ptr[panel + 1];
+  const int total = it1 > it0 + warp ? (it1 - it0 - warp + nw - 1) / nw : 0;  // items it0+warp+j*nw
+  int2 hb = lane < total ? __ldg(items + it0 + warp + lane * nw) : make_int2(0, 0);
+  LaneBuf cur, nxt;
+  int2 hc = make_int2(__shfl_sync(0xffffffffu, hb.x, 0), __shfl_sync(0xffffffffu, hb.y, 0));
+  if (total > 0) lane_load<false>(reinterpret_cast<const char *>(recs + (uint32_t)hc.x), hc, lane, cur);
+  for (int j = 0; j < total; ++j) {
+    int2 hn = make_int2(0, 0);
+    if (j + 1 < total) {
+      if (((j + 1) & 31) == 0) {  // next batch of 32 headers
+        const int k = j + 1 + lane;
+        hb = k < total ? __ldg(items + it0 + warp + k * nw) : make_int2(0, 0);
+      }
+      hn = make_int2(__shfl_sync(0xffffffffu, hb.x, (j + 1) & 31), __shfl_sync(0xffffffffu, hb.y, (j + 1) & 31));
+      lane_load<false>(reinterpret_cast<const char *>(recs + (uint32_t)hn.x), hn, lane, nxt);
+    }
+    dispatch_lane<KM, NB, 1, KM + 1>(hc.y & 0xff, cur, B, ldb, acc);
+    cur = nxt;
+    hc = hn;
+  }
+
+  float v[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) v[i] = (i < KM * NB) ? acc[i / NB][i % NB] : 0.f;
+  warp_transpose_reduce<V>(v, lane);
+  constexpr int kRep = 32 / V;
+  if ((lane % kRep) == 0) red[warp][transpose_reduce_index<V>(lane)] = v[0];
+  __syncthreads();
+  if (threadIdx.x < KM * NB) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += red[w][threadIdx.x];
+    const int k = threadIdx.x / NB, q = threadIdx.x % NB;
+    const int64_t row = (int64_t)panel * KM + k;
+    if (row < rows) {
+      float *c = C + row * ldc + q;
+      *c = accumulate ? *c + s : s;
+    }
+  }
+}
+
+// ------------------------------------- narrow B, B staged in shared memory ----
+// SpMV over lane blocks when the fp32 vector fits in shared memory.  The
+// random B-row gathers bound the kernels above: a warp load whose 32 lanes
+// touch 32 different 128-byte lines costs up to 32 L1 wavefronts, ~1 cycle
+// per entry per SM (config-5 SpMV: 7.9 M gathers, ~27 us; records resident in
+// L2 did not make it faster), while a random 4- or 8-byte shared-memory
+// gather costs a few bank-conflict wavefronts per warp.  Each CTA copies B
+// (K x N) into shared memory once; then every warp is an independent worker
+// over whole panels in the plan's heaviest-first order (panel t, t + T, ...
+// for T warps in the grid).  A warp's items stream through kXRing slots of
+// its own in shared memory, one cp.async.bulk per item with completion on
+// the slot's mbarrier, issued ahead across panel boundaries; the headers of
+// the items are read 32 at a time, one per lane.  Panel sums stay in
+// registers; one store per C element; no CTA barrier after the staging, no
+// atomics.  Every mbarrier wait is bounded: on expiry the warp records 7 in
+// *status, waits (bounded) for its copies still in flight, and stops.
+// `starve` (test hook) issues no copies, so that the first wait expires.
+constexpr int kLaneSlotBytes = 32 + 32 * (2 * kLaneSlots + 4 * kLaneSlots);  // largest item: 32 P=1 blocks
+constexpr int kXRing = 3;                                                   // slots per warp
+constexpr uint32_t kXWaitLimit = 1u << 20;                                 // polls of mbarrier.try_wait
+// 16-value lane blocks leave shared memory for 16 warps beside a 64 KB B
+constexpr int kXMaxThreads = kLaneSlots >= 16 ? 512 : 1024;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ bool xb_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool xb_wait(uint64_t *bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kXWaitLimit; ++i)
+    if (xb_try_wait(bar, parity)) return true;
+  return false;
+}
+
+template <int KM, int P, int NB>
+__device__ __forceinline__ void lane_compute_sp(const LaneBuf &b, const float *__restrict__ xs,
+                                                float (&acc)[KM][NB]) {
+  constexpr int U = lane_entries(P);
+  float t[P][NB];
+#pragma unroll
+  for (int p = 0; p < P; ++p)
+#pragma unroll
+    for (int q = 0; q < NB; ++q) t[p][q] = 0.f;
+  float x[U][NB];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const uint32_t c = (b.c[u >> 1] >> ((u & 1) * 16)) & 0xffffu;
+    if constexpr (NB == 1) {
+      x[u][0] = xs[c];
+    } else {
+      const float2 f = reinterpret_cast<const float2 *>(xs)[c];
+      x[u][0] = f.x; x[u][1] = f.y;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+#pragma unroll
+    for (int p = 0; p < P; ++p)
+#pragma unroll
+      for (int q = 0; q < NB; ++q) t[p][q] = fmaf(b.v[u * P + p], x[u][q], t[p][q]);
+  add_rows<KM, P, NB>((int)b.m, t, acc);
+}
+
+template <int KM, int NB, int LO, int HI>
+__device__ __forceinline__ void dispatch_lane_s(int P, const LaneBuf &b, const float *__restrict__ xs,
+                                                float (&acc)[KM][NB]) {
+  if constexpr (HI - LO == 1) {
+    lane_compute_sp<KM, LO, NB>(b, xs, acc);
+  } else {
+    constexpr int MID = (LO + HI) / 2;
+    if (P < MID) dispatch_lane_s<KM, NB, LO, MID>(P, b, xs, acc);
+    else dispatch_lane_s<KM, NB, MID, HI>(P, b, xs, acc);
+  }
+}
+
+// Dynamic shared memory of the staged kernel: B, then each warp's slots,
+// slot headers and mbarriers.
+__host__ __device__ constexpr size_t lane_x_bytes(int64_t kcols, int nb) {
+  return ((size_t)kcols * nb * 4 + 127) & ~(size_t)127;
+}
+__host__ __device__ constexpr size_t lane_x_smem(int64_t kcols, int nb, int warps) {
+  return lane_x_bytes(kcols, nb) + (size_t)warps * kXRing * (kLaneSlotBytes + 8 + 8);
+}
+
+template <int KM, int NB>
+__global__ void __launch_bounds__(kXMaxThreads)
+spmm_lane_x_kernel(const uint32_t *__restrict__ recs, const int2 *__restrict__ items,
+                   const int4 *__restrict__ pm, const int32_t *__restrict__ order, int64_t panels,
+                   const float *__restrict__ B, int64_t ldb, int64_t kcols, float *__restrict__ C, int64_t ldc,
+                   int64_t rows, int accumulate, int *status, int starve) {
+  static_assert(NB == 1 || NB == 2, "B staging is for N = 1 and 2");
+  constexpr int V = pow2_ceil(KM * NB);
+  static_assert(V <= 32, "KM*NB must not exceed 32");
+  extern __shared__ __align__(128) unsigned char smraw[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const size_t xb = lane_x_bytes(kcols, NB);
+  float *xs = reinterpret_cast<float *>(smraw);
+  unsigned char *ring = smraw + xb + (size_t)warp * kXRing * kLaneSlotBytes;
+  int2 *hdr = reinterpret_cast<int2 *>(smraw + xb + (size_t)nw * kXRing * kLaneSlotBytes) + warp * kXRing;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smraw + xb + (size_t)nw * kXRing * (kLaneSlotBytes + 8)) +
+                  warp * kXRing;
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < kXRing; ++r)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar + r)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+
+  // stage B (K x NB, row pitch ldb) as a dense K*NB array
+  const int64_t total_x = kcols * NB;
+  if (ldb == NB && (reinterpret_cast<uintptr_t>(B) & 15) == 0) {
+    const int64_t n4 = total_x >> 2;
+    for (int64_t i = threadIdx.x; i < n4; i += blockDim.x)
+      reinterpret_cast<float4 *>(xs)[i] = __ldg(reinterpret_cast<const float4 *>(B) + i);
+    for (int64_t i = (n4 << 2) + threadIdx.x; i < total_x; i += blockDim.x) xs[i] = __ldg(B + i);
+  } else {
+    for (int64_t i = threadIdx.x; i < total_x; i += blockDim.x) xs[i] = __ldg(B + (i / NB) * ldb + (i % NB));
+  }
+  __syncthreads();
+
+  const int64_t T = (int64_t)gridDim.x * nw;
+  // issue cursor (warp-uniform): panel position ti, its table entry mi, next
+  // item ii; the headers of items [ib0, ib0 + 32) sit one per lane in ib
+  int64_t ti = (int64_t)blockIdx.x * nw + warp;
+  if (ti >= panels) return;
+  int4 mi = __ldg(pm + order[ti]);
+  int ii = mi.x, ib0 = mi.x;
+  int2 ib = lane < mi.y - mi.x ? __ldg(items + mi.x + lane) : make_int2(0, 0);
+  int pn_next = ti + T < panels ? order[ti + T] : -1;  // panel after the issue cursor's
+  int in_flight = 0, slot_in = 0, slot_out = 0;
+  uint32_t phase = 0;  // bit r: parity of slot r's next completion
+  auto issue = [&]() {
+    while (in_flight < kXRing) {
+      while (ii >= mi.y) {  // next panel of this warp (empty panels have no items)
+        ti += T;
+        if (ti >= panels) return;
+        mi = __ldg(pm + pn_next);
+        pn_next = ti + T < panels ? order[ti + T] : -1;
+        ii = ib0 = mi.x;
+        ib = lane < mi.y - mi.x ? __ldg(items + mi.x + lane) : make_int2(0, 0);
+      }
+      if (ii - ib0 >= 32) {
+        ib0 = ii;
+        ib = lane < mi.y - ii ? __ldg(items + ii + lane) : make_int2(0, 0);
+      }
+      const int2 it = make_int2(__shfl_sync(0xffffffffu, ib.x, ii - ib0), __shfl_sync(0xffffffffu, ib.y, ii - ib0));
+      if (lane == 0 && !starve) {
+        const uint32_t bytes = lane_item_words(it.y >> 8, it.y & 0xff) * 4u;
+        hdr[slot_in] = it;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar + slot_in)),
+                     "r"(bytes)
+                     : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_addr(ring + slot_in * kLaneSlotBytes)),
+            "l"(recs + (uint32_t)it.x), "r"(bytes), "r"(smem_addr(bar + slot_in))
+            : "memory");
+      }
+      slot_in = slot_in + 1 == kXRing ? 0 : slot_in + 1;
+      ++in_flight;
+      ++ii;
+    }
+  };
+  issue();
+
+  for (int64_t t = (int64_t)blockIdx.x * nw + warp; t < panels; t += T) {
+    const int panel = order[t];
+    const int4 m = __ldg(pm + panel);
+    float acc[KM][NB];
+#pragma unroll
+    for (int k = 0; k < KM; ++k)
+#pragma unroll
+      for (int q = 0; q < NB; ++q) acc[k][q] = 0.f;
+    for (int j = m.x; j < m.y; ++j) {
+      if (!xb_wait(bar + slot_out, (phase >> slot_out) & 1u)) {
+        if (lane == 0) atomicExch(status, 7);
+        if (!starve)  // let the copies still in flight land before the CTA may exit
+          for (int k = 1; k < in_flight; ++k) {
+            const int r = (slot_out + k) % kXRing;
+            xb_wait(bar + r, (phase >> r) & 1u);
+          }
+        return;
+      }
+      __syncwarp();
+      const int2 it = hdr[slot_out];
+      LaneBuf b;
+      lane_load<true>(reinterpret_cast<const char *>(ring + slot_out * kLaneSlotBytes), it, lane, b);
+      __syncwarp();  // every lane has read the slot: it may be refilled
+      phase ^= 1u << slot_out;
+      slot_out = slot_out + 1 == kXRing ? 0 : slot_out + 1;
+      --in_flight;
+      issue();
+      dispatch_lane_s<KM, NB, 1, KM + 1>(it.y & 0xff, b, xs, acc);
+    }
+    float v[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = (i < KM * NB) ? acc[i / NB][i % NB] : 0.f;
+    warp_transpose_reduce<V>(v, lane);
+    constexpr int kRep = 32 / V;
+    const int idx = transpose_reduce_index<V>(lane);
+    if ((lane % kRep) == 0 && idx < KM * NB) {
+      const int k = idx / NB, q = idx % NB;
+      const int64_t row = (int64_t)panel * KM + k;
+      if (row < rows) {
+        float *c = C + row * ldc + q;
+        *c = accumulate ? *c + v[0] : v[0];
+      }
+    }
+  }
+}
+
+using LaneXFn = void (*)(const uint32_t *, const int2 *, const int4 *, const int32_t *, int64_t, const float *,
+                         int64_t, int64_t, float *, int64_t, int64_t, int, int *, int);
+
 using WideFn = void (*)(WideArgs, const WideArgs *, const int32_t *, int);
 using NarrowFn = void (*)(const uint32_t *, const int2 *, const int32_t *, const int32_t *, const float *,
                           int64_t, float *, int64_t, int64_t, int);
@@ -841,3 +1262,9 @@ sc::NarrowFn sc_narrow_kernel_km3(int nb, int vt);
 sc::NarrowFn sc_narrow_kernel_km4(int nb, int vt);
 sc::NarrowFn sc_narrow_kernel_km5(int nb, int vt);
 sc::NarrowFn sc_narrow_kernel_km6(int nb, int vt);
+sc::LaneXFn sc_lane_x_kernel_km1(int nb);
+sc::LaneXFn sc_lane_x_kernel_km2(int nb);
+sc::LaneXFn sc_lane_x_kernel_km3(int nb);
+sc::LaneXFn sc_lane_x_kernel_km4(int nb);
+sc::LaneXFn sc_lane_x_kernel_km5(int nb);
+sc::LaneXFn sc_lane_x_kernel_km6(int nb);

@@ -91,16 +91,19 @@ struct sc_plan {
   bool dense_bf16 = false;      // bf16 tiles (SC_PLAN_DENSE_BF16) instead of the fp32-exact splits
   int dense_mode = 0;           // sc::dense::kModeTf32x3 / kModeBf16 / kModeBf16x3
   int value_type = 0;           // stored values: 0 fp32, 1 fp16, 2 bf16 (compact small-B records)
-  int record_vt = 0;            // record layout the narrow kernel reads: value_type, or 3 = split blocks
+  int record_vt = 0;            // record layout the narrow kernel reads: value_type, 3 split blocks, 4 lane blocks
+  bool xstage = false;          // lane blocks read by the kernel that stages B in shared memory
+  int4 *panel_meta = nullptr;   // xstage: per panel {first item, end item, first word, end word} | status
   uint32_t flags = 0;           // SC_PLAN_* given at creation
   ~sc_plan() {
-    if (dev || stage_b || stage_c || a_tiles || chunk_order || side || khalf_items[0] || side2) {
+    if (dev || stage_b || stage_c || a_tiles || chunk_order || panel_meta || side || khalf_items[0] || side2) {
       int prev;
       bool ok = cudaGetDevice(&prev) == cudaSuccess;
       if (ok && prev != device) cudaSetDevice(device);
       if (dev) cudaFree(dev);
       if (a_tiles) cudaFree(a_tiles);  // one allocation: tiles | rb_ptr | rb_chunk | b_tiles | status
       if (chunk_order) cudaFree(chunk_order);
+      if (panel_meta) cudaFree(panel_meta);
       if (khalf_items[0]) cudaFree(khalf_items[0]);
       for (auto &e : host_ev)
         if (e) cudaEventDestroy(e);
@@ -119,6 +122,7 @@ namespace {
 
 using sc::WideFn;
 using sc::NarrowFn;
+using sc::LaneXFn;
 
 // Shared-memory carveout preference (percent) applied once per kernel;
 // SC_CARVEOUT overrides for tuning experiments (-1 = driver default).
@@ -157,6 +161,17 @@ WideFn wide_kernel_raw(int km, int vec, bool batch) {
 }
 WideFn wide_kernel(int km, int vec, bool batch) { return with_carveout(wide_kernel_raw(km, vec, batch)); }
 
+LaneXFn lane_x_kernel(int km, int nb) {
+  switch (km) {
+    case 1: return sc_lane_x_kernel_km1(nb);
+    case 2: return sc_lane_x_kernel_km2(nb);
+    case 3: return sc_lane_x_kernel_km3(nb);
+    case 4: return sc_lane_x_kernel_km4(nb);
+    case 5: return sc_lane_x_kernel_km5(nb);
+    default: return sc_lane_x_kernel_km6(nb);
+  }
+}
+
 NarrowFn narrow_kernel(int km, int nb, int vt) {
   switch (km) {
     case 1: return sc_narrow_kernel_km1(nb, vt);
@@ -168,10 +183,41 @@ NarrowFn narrow_kernel(int km, int nb, int vt) {
   }
 }
 
-bool split_records_enabled() {
-  static const bool v = [] {
-    const char *e = getenv("SC_SPLIT_RECORDS");
-    return !(e && e[0] == '0');
+// Record layout of fp32 small-B plans with K <= 65536: lane blocks where the
+// kernel that stages B in shared memory applies (SpMV, K fp32 within
+// kXStageMaxBytes, at least xstage_min_panels() panels), split item blocks
+// otherwise (N = 2 staged measured no faster than split blocks: 35.0 vs
+// 34.8 us on the config-5 matrix).  SC_NARROW_LAYOUT=lane / split / rec (interleaved records; also
+// SC_SPLIT_RECORDS=0) forces one (measurement switch).
+constexpr int64_t kXStageMaxBytes = 160 * 1024;
+int narrow_layout_override() {
+  static const int v = [] {
+    const char *r = getenv("SC_SPLIT_RECORDS");
+    if (r && r[0] == '0') return 0;
+    const char *e = getenv("SC_NARROW_LAYOUT");
+    if (e && strcmp(e, "rec") == 0) return 0;
+    if (e && strcmp(e, "split") == 0) return 3;
+    if (e && strcmp(e, "lane") == 0) return 4;
+    return -1;
+  }();
+  return v;
+}
+// Panels from which the staged kernel is used (small matrices keep one CTA
+// per panel: a warp per panel leaves too few warps busy); SC_XSTAGE_MIN_PANELS.
+int64_t xstage_min_panels() {
+  static const int64_t v = [] {
+    const char *e = getenv("SC_XSTAGE_MIN_PANELS");
+    return (int64_t)(e ? atoll(e) : 1024);
+  }();
+  return v;
+}
+// Threads per CTA of the staged kernel (at most its launch bound);
+// SC_XSTAGE_THREADS overrides it for tuning experiments.
+int xstage_threads() {
+  static const int v = [] {
+    const char *e = getenv("SC_XSTAGE_THREADS");
+    const int x = e ? atoi(e) : sc::kXMaxThreads;
+    return (x >= 32 && x <= sc::kXMaxThreads && x % 32 == 0) ? x : sc::kXMaxThreads;
   }();
   return v;
 }
@@ -479,8 +525,18 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   // fp32 small-B plans with K <= 65536: split item blocks (16-bit columns,
   // then exactly P values per entry); SC_SPLIT_RECORDS=0 keeps the
   // interleaved records (measurement switch).
-  const bool split = !compact && (n == 1 || n == 2 || n == 4) && cf.num_cols <= 65536 && split_records_enabled();
-  plan->record_vt = split ? 3 : plan->value_type;
+  int layout = 0;
+  bool xstage = false;
+  if (!compact && (n == 1 || n == 2 || n == 4) && cf.num_cols <= 65536) {
+    xstage = n == 1 && (int64_t)cf.num_cols * 4 <= kXStageMaxBytes && (pe - pb) >= xstage_min_panels();
+    layout = narrow_layout_override();
+    if (layout < 0) layout = xstage ? 4 : 3;
+    xstage = xstage && layout == 4;
+  }
+  plan->xstage = xstage;
+  const bool split = layout == 3;
+  const bool lanes = layout == 4;
+  plan->record_vt = layout != 0 ? layout : plan->value_type;
   if (compact) {
     require(n == 1 || n == 2 || n == 4, SC_ERR_UNSUPPORTED,
             "16-bit value records are for the small-B / SpMV kernel (n_cols_b 1, 2 or 4)");
@@ -500,6 +556,12 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
   std::vector<int2> items;
   std::vector<int32_t> item_ptr(plan->panels + 1, 0);
   std::vector<int64_t> work(plan->panels, 0);
+  struct LaneGroup {
+    std::vector<uint8_t> masks;  // per block
+    std::vector<uint32_t> cols;  // 16 per block
+    std::vector<uint32_t> vals;  // kLaneSlots per block
+  };
+  std::vector<LaneGroup> lane_groups(km + 1);
   for (int64_t lp = 0; lp < plan->panels; ++lp) {
     const int64_t gp = pb + lp;
     for (int g = 0; g < np; ++g) {
@@ -510,6 +572,22 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
       int64_t seg_len = 0;
       std::vector<uint32_t> seg_cols, seg_vals;  // split mode: the segment's columns and value bits
       auto close_items = [&]() {
+        if (lanes) {  // blocks of U entries of this mask, emitted per popcount at the panel's end
+          const int U = sc::lane_entries(P);
+          LaneGroup &lg = lane_groups[P];
+          for (int64_t e = 0; e < seg_len; e += U) {
+            const int len = (int)std::min<int64_t>(U, seg_len - e);
+            lg.masks.push_back((uint8_t)rowbits[g]);
+            const size_t c0 = lg.cols.size(), v0 = lg.vals.size();
+            lg.cols.resize(c0 + 16, 0u);
+            lg.vals.resize(v0 + sc::kLaneSlots, 0u);
+            for (int i = 0; i < len; ++i) {
+              lg.cols[c0 + i] = seg_cols[e + i];
+              for (int q = 0; q < P; ++q) lg.vals[v0 + (size_t)i * P + q] = seg_vals[(e + i) * P + q];
+            }
+          }
+          return;
+        }
         if (split) {
           for (int64_t e = 0; e < seg_len; e += item_cap) {
             const int len = (int)std::min<int64_t>(item_cap, seg_len - e);
@@ -537,7 +615,7 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
         if (all_pad) continue;
         const int32_t col = pt.cb[j];
         require(col >= 0 && col < cf.num_cols, SC_ERR_FORMAT, "column index out of range in CF");
-        if (split) {
+        if (split || lanes) {
           seg_cols.push_back((uint32_t)col);
           for (int p = 0; p < P; ++p) {
             const float v = pt.vals[(size_t)j * P + p];
@@ -586,6 +664,34 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
         work[lp] += P + 2;
       }
       if (seg_len > 0) close_items();
+    }
+    if (lanes) {
+      for (int P = 1; P <= km; ++P) {
+        LaneGroup &lg = lane_groups[P];
+        const int nblk = (int)lg.masks.size();
+        for (int b0 = 0; b0 < nblk; b0 += 32) {
+          const int nl = std::min(32, nblk - b0);
+          while (recs.size() % 4) recs.push_back(0);
+          const int64_t off = (int64_t)recs.size();
+          require(off < (int64_t)INT32_MAX, SC_ERR_UNSUPPORTED, "record stream exceeds 8 GiB");
+          recs.resize(recs.size() + sc::lane_item_words(nl, P), 0u);
+          uint8_t *mk = reinterpret_cast<uint8_t *>(recs.data() + off);
+          uint32_t *cw = recs.data() + off + 8;
+          uint32_t *vw = cw + sc::lane_col_region(nl, P) / 4;
+          for (int l = 0; l < nl; ++l) {
+            const int blk = b0 + l;
+            mk[l] = lg.masks[blk];
+            for (int u = 0; u < sc::lane_entries(P); ++u)
+              cw[sc::lane_col_word(nl, P, l, u)] |= lg.cols[(size_t)blk * 16 + u] << (16 * (u % 2));
+            for (int q = 0; q < sc::kLaneSlots; ++q)  // chunk-major: chunk c of lane l at words (c * nl + l) * 4
+              vw[((size_t)(q / 4) * nl + l) * 4 + q % 4] = lg.vals[(size_t)blk * sc::kLaneSlots + q];
+          }
+          items.push_back(make_int2((int)off, P | (nl << 8)));
+        }
+        lg.masks.clear();
+        lg.cols.clear();
+        lg.vals.clear();
+      }
     }
     item_ptr[lp + 1] = (int32_t)items.size();
     work[lp] += 4 * (item_ptr[lp + 1] - item_ptr[lp]);
@@ -636,6 +742,8 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
                                    (double)plan->items / (double)plan->panels, plan->warps);
   if (const char *e = getenv("SC_WIDE_WARPS"))  // tuning experiments: fixed warps per panel
     if (plan->kernel == 2 && atoi(e) >= 1 && atoi(e) <= 8) plan->warps = atoi(e);
+  if (const char *e = getenv("SC_NARROW_WARPS"))  // tuning experiments: fixed warps per panel
+    if (plan->kernel == 1 && atoi(e) >= 1 && atoi(e) <= 8) plan->warps = atoi(e);
   auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
   const size_t b_recs = align(recs.size() * 4);
   const size_t b_items = align(std::max<size_t>(1, items.size()) * sizeof(int2));
@@ -658,6 +766,25 @@ sc_plan *build_plan(const sc_cf &cf, int32_t n, int32_t device, int64_t pb, int6
     cuda_check(cudaMemcpy(base + b_recs + b_items + b_ptr, order.data(), order.size() * 4,
                           cudaMemcpyHostToDevice),
                "upload panel order");
+  if (plan->xstage) {
+    std::vector<int4> pmh(std::max<int64_t>(1, plan->panels), make_int4(0, 0, 0, 0));
+    for (int64_t i = 0; i < plan->panels; ++i) {
+      const int a = item_ptr[i], b = item_ptr[i + 1];
+      int w0 = 0, w1 = 0;
+      if (b > a) {
+        const int2 l = items[b - 1];
+        w0 = items[a].x;
+        w1 = l.x + (int)sc::lane_item_words(l.y >> 8, l.y & 0xff);
+      }
+      pmh[i] = make_int4(a, b, w0, w1);
+    }
+    // one allocation: panel table | status word of the staged kernel's bounded waits
+    cuda_check(cudaMalloc(&plan->panel_meta, (pmh.size() + 1) * sizeof(int4)), "cudaMalloc(panel table)");
+    cuda_check(cudaMemcpy(plan->panel_meta, pmh.data(), pmh.size() * sizeof(int4), cudaMemcpyHostToDevice),
+               "upload panel table");
+    plan->status = reinterpret_cast<int *>(plan->panel_meta + pmh.size());
+    cuda_check(cudaMemset(plan->status, 0, sizeof(int4)), "clear status");
+  }
   if (plan->kernel == 2 && plan->rows > 0 && use_dense(*plan, cf)) build_dense(*plan, cf, pb, rowbits);
   if (plan->kernel == 2 && plan->cols >= 4096 && plan->panels > 0) build_ksplit(*plan, recs, items, item_ptr);
   if (plan->kernel != 3 && plan->panels >= sc_plan::kHostChunks) {
@@ -724,7 +851,43 @@ void launch_panels(sc_plan *p, const float *B, int64_t ldb, float *C, int64_t ld
     cuda_check((cudaError_t)e, "dense tile kernel launch");
     return;
   }
-  if (p->kernel == 1) {
+  if (p->kernel == 1 && p->xstage) {
+    // B staged in shared memory; persistent CTAs whose warps stream whole panels
+    LaneXFn fn = lane_x_kernel((int)p->km, nb);
+    int dev = 0, sms = 0, smem_max = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    // warps per CTA: what shared memory allows, but no more than spreads the
+    // panels over every SM (a warp takes whole panels)
+    int warps = xstage_threads() / 32;
+    while (warps > 1 && sc::lane_x_smem(p->cols, nb, warps) > (size_t)smem_max) --warps;
+    warps = (int)std::max<int64_t>(1, std::min<int64_t>(warps, (count + sms - 1) / std::max(1, sms)));
+    const size_t smem = sc::lane_x_smem(p->cols, nb, warps);
+    require(smem <= (size_t)smem_max, SC_ERR_UNSUPPORTED, "B does not fit in shared memory");
+    {
+      // raise the kernel's dynamic shared memory limit once per (device, kernel, size)
+      static std::mutex mu;
+      static std::vector<std::pair<std::pair<int, const void *>, size_t>> done;
+      std::lock_guard<std::mutex> lk(mu);
+      size_t *have = nullptr;
+      for (auto &d : done)
+        if (d.first.first == dev && d.first.second == (const void *)fn) have = &d.second;
+      if (!have || *have < smem) {
+        cuda_check(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                   "shared memory size of the staged kernel");
+        if (have) *have = smem;
+        else done.push_back({{dev, (const void *)fn}, smem});
+      }
+    }
+    int per_sm = 0;
+    cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 32 * warps, smem), "occupancy");
+    const int64_t want = (count + warps - 1) / warps;
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)std::max(1, per_sm) * sms));
+    fn<<<dim3((unsigned)grid), 32 * warps, smem, stream>>>(p->recs, p->item_list, p->panel_meta, order, count, B,
+                                                           ldb, p->cols, C, ldc, p->rows, accumulate, p->status,
+                                                           (p->flags & SC_PLAN_TEST_STARVE) ? 1 : 0);
+  } else if (p->kernel == 1) {
     if (ldb % nb == 0 && aligned(B, 4 * nb)) {
       NarrowFn fn = narrow_kernel((int)p->km, nb, p->record_vt);
       fn<<<dim3((unsigned)count), threads, 0, stream>>>(p->recs, p->item_list, p->item_ptr, order, B, ldb, C, ldc,
@@ -797,7 +960,7 @@ void check_plan_status(sc_plan *p) {
   if (!p->status) return;
   const int v = take_status(p->status);
   if (v)
-    throw sc_error(SC_ERR_DEVICE, "dense-tile kernel: a bounded device wait expired (status " + std::to_string(v) +
+    throw sc_error(SC_ERR_DEVICE, "product kernel: a bounded device wait expired (status " + std::to_string(v) +
                                       "); C is incomplete");
 }
 

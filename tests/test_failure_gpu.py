@@ -91,6 +91,33 @@ def test_dense_wait_expiry_is_reported(cuda):
     _small_product_ok(cuda)
 
 
+def test_staged_small_b_wait_expiry_is_reported(cuda):
+    """Staged small-B kernel (SpMV of a large matrix) with its record copies
+    starved: every warp's bounded mbarrier wait expires, C stays untouched,
+    the status is 7 once, and the host entry point returns SC_ERR_DEVICE."""
+    import torch
+    from sparse_computation_b200.partition import row_slice
+    a, B = wl.config5(n_cols_b=1)
+    a = row_slice(a, 0, 4096)
+    cf = sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1)
+    plan = sc.SpMMPlan(cf, 1, flags=sc.SC_PLAN_TEST_STARVE)
+    C = torch.full((a[0], 1), 123.0, device=cuda)
+    t0 = time.perf_counter()
+    plan.spmm(torch.from_numpy(B).to(cuda), C)
+    assert plan.status() == 7
+    assert time.perf_counter() - t0 < 60.0
+    assert plan.status() == 0
+    assert bool(torch.all(C == 123.0))
+    with pytest.raises(sc.ScError) as ei:
+        plan.spmm_host(B)
+    assert ei.value.code == sc.SC_ERR_DEVICE
+    ok = sc.SpMMPlan(cf, 1)
+    y = ok.spmm(torch.from_numpy(B).to(cuda))
+    assert ok.status() == 0
+    assert_parity(y.cpu().numpy(), a, B)
+    _small_product_ok(cuda)
+
+
 def test_batch_status_clean(cuda):
     import torch
     mats = wl.config4(128)[:4]

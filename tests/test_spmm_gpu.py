@@ -256,7 +256,7 @@ def test_config5_full_size_parity(cuda):
     assert np.all(np.abs(lhs - rhs) <= 3 * RTOL * scale2)
 
 
-@pytest.mark.parametrize("N", [1, 4])
+@pytest.mark.parametrize("N", [1, 2, 4])
 def test_config5_small_b_full_size_parity(cuda, N):
     """The config-5 matrix on the small-B kernel (SpMV and N = 4): every row
     against the oracle at the fp32 bound."""
@@ -272,6 +272,35 @@ def test_config5_small_b_full_size_parity(cuda, N):
     ref = cpu.spmm_csr_float(ip, ix, dx, B)
     scale = cpu.spmm_csr_abs(ip, ix, dx, B)
     assert np.all(np.abs(y.astype(np.float64) - ref) <= RTOL * scale)
+
+
+def test_staged_small_b_kernel_m_sweep(cuda):
+    """The kernel that stages B in shared memory (SpMV of large matrices) at
+    every kernel_m, with a strided B and C and in accumulate mode, against
+    the oracle at the fp32 bound.  6144 rows give >= 1024 panels at every
+    kernel_m, so every plan here takes the staged kernel."""
+    import torch
+    from sparse_computation_b200.partition import row_slice
+    N = 1
+    a, B = wl.config5(n_cols_b=N)
+    a = row_slice(a, 0, 6144)
+    _, _, ip, ix, dx = a
+    ref = cpu.spmm_csr_float(ip, ix, dx, B)
+    scale = cpu.spmm_csr_abs(ip, ix, dx, B)
+    C0 = wl.dense_b(a[0], N, 11)
+    for km in range(1, 7):
+        plan = sc.SpMMPlan(sc.csr_to_compressed_format_converter(to_csr_handle(a), km, 1), N)
+        Bw = torch.zeros((B.shape[0], N + 3), device=cuda)
+        Bw[:, :N] = torch.from_numpy(B).to(cuda)
+        Cw = torch.full((a[0], N + 5), 7.0, device=cuda)
+        Cw[:, :N] = torch.from_numpy(C0).to(cuda)
+        plan.spmm(Bw[:, :N], Cw[:, :N], accumulate=True)
+        y = Cw[:, :N].cpu().numpy().astype(np.float64)
+        assert np.all(np.abs(y - (ref + C0)) <= RTOL * (scale + np.abs(C0))), km
+        assert torch.all(Cw[:, N:] == 7.0)
+        assert plan.status() == 0
+        y2 = plan.spmm(torch.from_numpy(B).to(cuda)).cpu().numpy().astype(np.float64)
+        assert np.all(np.abs(y2 - ref) <= RTOL * scale), km
 
 
 def test_batch_layer_stack_one_launch(cuda):
