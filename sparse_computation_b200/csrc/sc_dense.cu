@@ -11,7 +11,9 @@
 //              32w..32w+31 = C rows), then row-contiguous stores of C.
 // Every wait on an mbarrier is bounded; on expiry the CTA records an error in
 // *status, stops issuing work, and still releases its tensor memory.
+#include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 
 #include <cooperative_groups.h>
@@ -333,6 +335,261 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
   }
 }
 
+// The MMAs of one stage (one kept K-chunk) into the accumulator at `acc`;
+// `first`: the stage starts the accumulator.
+template <int MODE>
+__device__ __forceinline__ void mma_stage(uint32_t acc, uint32_t base, bool first) {
+  if constexpr (MODE == kModeBf16x3) {
+    uint64_t a[3], b[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      a[j] = sdesc(base + j * kTileBytes);
+      b[j] = sdesc(base + (3 + j) * kTileBytes);
+    }
+#pragma unroll
+    for (int k = 0; k < kBKb / 16; ++k) {
+      const uint64_t step = (uint64_t)((k * 32) >> 4);
+      mma_bf16(acc, a[2] + step, b[0] + step, (!first || k > 0) ? 1u : 0u);
+      mma_bf16(acc, a[0] + step, b[2] + step, 1u);
+      mma_bf16(acc, a[1] + step, b[1] + step, 1u);
+      mma_bf16(acc, a[1] + step, b[0] + step, 1u);
+      mma_bf16(acc, a[0] + step, b[1] + step, 1u);
+      mma_bf16(acc, a[0] + step, b[0] + step, 1u);
+    }
+  } else if constexpr (MODE == kModeBf16) {
+    const uint64_t a = sdesc(base), b = sdesc(base + kTileBytes);
+#pragma unroll
+    for (int k = 0; k < kBKb / 16; ++k) {
+      const uint64_t step = (uint64_t)((k * 32) >> 4);
+      mma_bf16(acc, a + step, b + step, (!first || k > 0) ? 1u : 0u);
+    }
+  } else {
+    const uint64_t a_hi = sdesc(base), a_lo = sdesc(base + kTileBytes);
+    const uint64_t b_hi = sdesc(base + 2 * kTileBytes), b_lo = sdesc(base + 3 * kTileBytes);
+#pragma unroll
+    for (int k = 0; k < kBK / 8; ++k) {
+      const uint64_t step = (uint64_t)((k * 32) >> 4);
+      mma_tf32(acc, a_lo + step, b_hi + step, (!first || k > 0) ? 1u : 0u);
+      mma_tf32(acc, a_hi + step, b_lo + step, 1u);
+      mma_tf32(acc, a_hi + step, b_hi + step, 1u);
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Persistent form for tasks not split over a cluster: one CTA per SM.  Its
+// producer thread takes task tickets from a counter in global memory
+// (status[1]; heaviest tasks first, so SMs that finish early take more) and
+// passes them to the MMA issuer and the epilogue warps through a four-entry
+// queue in shared memory; the last CTA to finish resets the counter
+// (status[2] counts finished CTAs).  Warp 0 (one thread) bulk-copies the
+// stages of its tasks through the ring without a break between tasks;
+// warp 1 (one thread) issues the MMAs into two 128-column accumulators in
+// tensor memory, alternating per task; warps 2-5 drain the finished
+// accumulator (warp w reads TMEM lanes 32*(w%4) ..) and store C while the
+// next task's stages load and multiply.  Every wait is bounded; on expiry the
+// CTA records 1 (producer), 2 (MMA issuer) or 3 (epilogue) in *status (the
+// first error stays), stores nothing more, and still frees its tensor memory.
+constexpr int kPersistThreads = 192;
+constexpr int kTaskQ = 4;
+template <bool BATCH, int MODE>
+__global__ void __launch_bounds__(kPersistThreads, 1)
+dense_gemm_persist_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *__restrict__ tasks,
+                          int64_t ntasks, int accumulate, int *status) {
+  constexpr int NST = MODE == kModeBf16 ? 6 : (MODE == kModeBf16x3 ? 2 : kStages);
+  constexpr int SB = 2 * mode_images(MODE) * kTileBytes;
+  constexpr int OP = mode_images(MODE) * kTileBytes;  // bytes of one operand's images
+  extern __shared__ __align__(1024) uint8_t dsmem[];
+  uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[NST], empty_bar[NST], acc_full[2], acc_empty[2], done_bar;
+  __shared__ __align__(8) uint64_t tq_full[kTaskQ], tq_empty[kTaskQ];
+  __shared__ int tq[kTaskQ];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int *ctr = status + 1, *done = status + 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    for (int q = 0; q < kTaskQ; ++q) {
+      mbar_init(&tq_full[q], 1);
+      mbar_init(&tq_empty[q], 5);  // the MMA issuer and the four epilogue warps
+    }
+    mbar_init(&done_bar, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(2 * kBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (threadIdx.x == 0) {
+    // producer: stage counter g runs over all kept chunks of all this CTA's tasks
+    uint32_t g = 0;
+    for (int j = 0;; ++j) {
+      const int q = j & (kTaskQ - 1);
+      if (j >= kTaskQ && !mbar_wait(&tq_empty[q], ((j / kTaskQ) - 1) & 1, &abort_flag)) {
+        atomicCAS(status, 0, 1);
+        abort_flag = 1;
+        break;
+      }
+      const int t = atomicAdd(ctr, 1);
+      tq[q] = t < ntasks ? t : -1;
+      mbar_arrive(&tq_full[q]);
+      if (t >= ntasks) break;
+      const int4 task = tasks[t];
+      DenseMat m;
+      if constexpr (BATCH) m = mats[task.x];
+      else m = one;
+      if (m.starve) continue;  // test hook: no copies, the MMA issuer's wait expires
+      const int c0 = m.rb_ptr[task.y], c1 = m.rb_ptr[task.y + 1];
+      for (int ci = c0; ci < c1; ++ci, ++g) {
+        const int s = (int)(g % NST);
+        if (g >= (uint32_t)NST && !mbar_wait(&empty_bar[s], ((g / NST) - 1) & 1, &abort_flag)) {
+          atomicCAS(status, 0, 1);
+          abort_flag = 1;
+          break;
+        }
+        uint8_t *st = ring + (size_t)s * SB;
+        const uint8_t *at = m.a_tiles + (size_t)ci * OP;
+        const uint8_t *bt = m.b_tiles + ((size_t)task.z * m.k_chunks + m.rb_chunk[ci]) * OP;
+        mbar_expect_tx(&full_bar[s], SB);
+        bulk_copy(st, at, OP, &full_bar[s]);
+        bulk_copy(st + OP, bt, OP, &full_bar[s]);
+      }
+      if (abort_flag) break;
+    }
+    // every CTA has taken its last ticket once all have counted themselves here
+    if (atomicAdd(done, 1) == (int)gridDim.x - 1) {
+      atomicExch(ctr, 0);
+      atomicExch(done, 0);
+    }
+  } else if (threadIdx.x == 32) {
+    // MMA issuer
+    uint32_t g = 0;
+    for (int j = 0;; ++j) {
+      const int q = j & (kTaskQ - 1);
+      if (!mbar_wait(&tq_full[q], (j / kTaskQ) & 1, &abort_flag)) {
+        atomicCAS(status, 0, 2);
+        abort_flag = 1;
+        break;
+      }
+      const int t = tq[q];
+      mbar_arrive(&tq_empty[q]);
+      if (t < 0) break;
+      const int4 task = tasks[t];
+      DenseMat m;
+      if constexpr (BATCH) m = mats[task.x];
+      else m = one;
+      const int a = j & 1;
+      if (j >= 2 && !mbar_wait(&acc_empty[a], ((j >> 1) - 1) & 1, &abort_flag)) {
+        atomicCAS(status, 0, 2);
+        abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int nk = m.rb_ptr[task.y + 1] - m.rb_ptr[task.y];
+      bool ok = true;
+      for (int i = 0; i < nk; ++i, ++g) {
+        const int s = (int)(g % NST);
+        if (!mbar_wait(&full_bar[s], (g / NST) & 1, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        mma_stage<MODE>(tmem + (uint32_t)(a * kBN), smem_u32(ring + (size_t)s * SB), i == 0);
+        mma_commit(&empty_bar[s]);  // stage free once these MMAs have read it
+      }
+      if (!ok) {
+        atomicCAS(status, 0, 2);
+        abort_flag = 1;
+        break;
+      }
+      mma_commit(&acc_full[a]);  // accumulator a complete (arrives at once when nk == 0)
+    }
+    mma_commit(&done_bar);  // every MMA issued here has completed
+  } else if (warp >= 2) {
+    // epilogue
+    const int qr = warp & 3;  // TMEM lanes 32qr .. 32qr + 31 = tile rows
+    for (int j = 0;; ++j) {
+      const int q = j & (kTaskQ - 1);
+      if (!mbar_wait(&tq_full[q], (j / kTaskQ) & 1, &abort_flag)) {
+        if (lane == 0) atomicCAS(status, 0, 3);
+        abort_flag = 1;
+        break;
+      }
+      const int t = tq[q];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tq_empty[q]);
+      if (t < 0) break;
+      const int4 task = tasks[t];
+      DenseMat m;
+      if constexpr (BATCH) m = mats[task.x];
+      else m = one;
+      const int a = j & 1;
+      if (!mbar_wait(&acc_full[a], (j >> 1) & 1, &abort_flag)) {
+        if (lane == 0) atomicCAS(status, 0, 3);
+        abort_flag = 1;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      const bool have = m.rb_ptr[task.y + 1] > m.rb_ptr[task.y];
+      const int64_t row = (int64_t)task.y * kBM + qr * 32 + lane;
+      const uint32_t trow = tmem + (uint32_t)(a * kBN) + ((uint32_t)(qr * 32) << 16);
+#pragma unroll 1
+      for (int cb = 0; cb < kBN / 32; ++cb) {
+        float v[32];
+        if (have) tmem_ld32(trow + (uint32_t)(cb * 32), v);
+        else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+        if (row < m.rows && !abort_flag) {
+          float *c = m.C + row * m.ldc + task.z * kBN + cb * 32;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            if (accumulate) {
+              const float4 x = *reinterpret_cast<const float4 *>(c + i);
+              o.x += x.x; o.y += x.y; o.z += x.z; o.w += x.w;
+            }
+            *reinterpret_cast<float4 *>(c + i) = o;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+  // free tensor memory only after the MMAs issued here have completed
+  if (threadIdx.x == 32) mbar_wait(&done_bar, 0, nullptr);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kBN));
+  }
+}
+
 // Rows [kc*BK, kc*BK + BK) x columns [nt*128, nt*128 + 128) of B into T (zero
 // past K or N).  With 16-byte aligned rows every thread issues its BK/8
 // float4 loads together (the scalar form left this kernel latency-bound);
@@ -481,6 +738,15 @@ int sc_dense_split_b(const sc::dense::DenseMat &one, const sc::dense::DenseMat *
   return (int)cudaGetLastError();
 }
 
+// SC_DENSE_PERSIST=0 keeps one CTA per task (measurement switch).
+static bool persist_enabled() {
+  static const bool v = [] {
+    const char *e = getenv("SC_DENSE_PERSIST");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
 int sc_dense_gemm(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mats, const int4 *tasks,
                   int64_t ntasks, int split, int mode, int accumulate, int *status, cudaStream_t s) {
   using namespace sc::dense;
@@ -493,6 +759,29 @@ int sc_dense_gemm(const sc::dense::DenseMat &one, const sc::dense::DenseMat *mat
                           {dense_gemm_kernel<true, kModeTf32x3>, dense_gemm_kernel<true, kModeBf16>,
                            dense_gemm_kernel<true, kModeBf16x3>}};
   const Fn fn = table[mats ? 1 : 0][mode];
+  if (split == 1 && persist_enabled()) {
+    // persistent kernel: one CTA per SM over the tasks, double-buffered accumulator
+    using PFn = void (*)(DenseMat, const DenseMat *, const int4 *, int64_t, int, int *);
+    const PFn ptable[2][3] = {
+        {dense_gemm_persist_kernel<false, kModeTf32x3>, dense_gemm_persist_kernel<false, kModeBf16>,
+         dense_gemm_persist_kernel<false, kModeBf16x3>},
+        {dense_gemm_persist_kernel<true, kModeTf32x3>, dense_gemm_persist_kernel<true, kModeBf16>,
+         dense_gemm_persist_kernel<true, kModeBf16x3>}};
+    const PFn pfn = ptable[mats ? 1 : 0][mode];
+    static std::atomic<unsigned> pattr_done[6];
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    std::atomic<unsigned> &bits = pattr_done[(mats ? 1 : 0) + 2 * mode];
+    if (dev >= 32 || !(bits.load() & (1u << dev))) {
+      cudaError_t e = cudaFuncSetAttribute(pfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return (int)e;
+      if (dev < 32) bits.fetch_or(1u << dev);
+    }
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(ntasks, sms));
+    pfn<<<(unsigned)grid, kPersistThreads, smem, s>>>(one, mats, tasks, ntasks, accumulate, status);
+    return (int)cudaGetLastError();
+  }
   // one bit per device ordinal (< 32); concurrent callers may both set the
   // attribute, which is harmless, and the bit update is atomic
   static std::atomic<unsigned> attr_done[6];

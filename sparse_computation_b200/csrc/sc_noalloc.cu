@@ -84,7 +84,7 @@ __global__ void noalloc_init(int rbs, int kcs, int nts, int32_t *rb_ptr, int32_t
   if (t <= rbs) rb_ptr[t] = (int32_t)(t * kcs);
   if (t < (int64_t)rbs * kcs) rb_chunk[t] = (int32_t)(t % kcs);
   if (t < (int64_t)rbs * nts) tasks[t] = make_int4(0, (int)(t / nts), (int)(t % nts), kcs);
-  if (t == 0) *status = 0;
+  if (t < 4) status[t] = 0;  // status | task counter | done counter of the dense kernel
 }
 
 size_t align1k(size_t x) { return (x + 1023) & ~(size_t)1023; }

@@ -396,7 +396,7 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
   cuda_check(cudaMemcpy(p.rb_ptr, rb_ptr.data(), rb_ptr.size() * 4, cudaMemcpyHostToDevice), "upload tiles");
   if (!rb_chunk.empty())
     cuda_check(cudaMemcpy(p.rb_chunk, rb_chunk.data(), rb_chunk.size() * 4, cudaMemcpyHostToDevice), "upload tiles");
-  cuda_check(cudaMemset(p.status, 0, 4), "clear status");
+  cuda_check(cudaMemset(p.status, 0, 16), "clear status");  // status | task counter | done counter
   p.row_blocks = rbs;
   p.kept_chunks = (int64_t)rb_chunk.size();
   p.dev_bytes += o_status + 1024;
@@ -1344,7 +1344,7 @@ int sc_batch_create(sc_plan *const *plans, int32_t count, sc_batch **out) {
   b->dmats = reinterpret_cast<sc::dense::DenseMat *>(base + bd + bo);
   b->dtasks = reinterpret_cast<int4 *>(base + bd + bo + bm);
   b->status = reinterpret_cast<int *>(base + bd + bo + bm + bt);
-  cuda_check(cudaMemset(b->status, 0, 4), "clear status");
+  cuda_check(cudaMemset(b->status, 0, 16), "clear status");  // status | task counter | done counter
   std::vector<int2> ord(tasks.size());
   for (size_t i = 0; i < tasks.size(); ++i) ord[i] = tasks[i].second;
   if (!ord.empty())
