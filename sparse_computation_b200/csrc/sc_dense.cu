@@ -17,6 +17,7 @@
 #include <cstring>
 
 #include <cooperative_groups.h>
+#include <cuda_bf16.h>
 
 #include "sc_dense.cuh"
 
@@ -703,14 +704,24 @@ __global__ void __launch_bounds__(256) split_b_bf16x3_kernel(DenseMat one, const
   for (int q = threadIdx.x; q < kBN * 8; q += blockDim.x) {
     const int n = q >> 3, c = q & 7;
     const int k0 = (c ^ (n & 7)) << 3;
+    // the same three parts as bf16x3_split (round to nearest even at each
+    // step), from the hardware conversion: two values per instruction
     uint32_t w[3][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      uint16_t lo[3], hi[3];
-      bf16x3_split(T[k0 + 2 * j][n], lo);
-      bf16x3_split(T[k0 + 2 * j + 1][n], hi);
-#pragma unroll
-      for (int r = 0; r < 3; ++r) w[r][j] = (uint32_t)lo[r] | ((uint32_t)hi[r] << 16);
+      const float2 x = make_float2(T[k0 + 2 * j][n], T[k0 + 2 * j + 1][n]);
+      const __nv_bfloat162 p1 = __floats2bfloat162_rn(x.x, x.y);
+      const float2 f1 = __bfloat1622float2(p1);
+      // inf / nan (or rounded up to inf): no tail parts
+      const bool okx = (__bfloat16_as_ushort(p1.x) & 0x7f80u) != 0x7f80u;
+      const bool oky = (__bfloat16_as_ushort(p1.y) & 0x7f80u) != 0x7f80u;
+      const float2 r1 = make_float2(okx ? x.x - f1.x : 0.f, oky ? x.y - f1.y : 0.f);
+      const __nv_bfloat162 p2 = __floats2bfloat162_rn(r1.x, r1.y);
+      const float2 f2 = __bfloat1622float2(p2);
+      const __nv_bfloat162 p3 = __floats2bfloat162_rn(r1.x - f2.x, r1.y - f2.y);
+      w[0][j] = *reinterpret_cast<const uint32_t *>(&p1);
+      w[1][j] = *reinterpret_cast<const uint32_t *>(&p2);
+      w[2][j] = *reinterpret_cast<const uint32_t *>(&p3);
     }
 #pragma unroll
     for (int r = 0; r < 3; ++r) img[r * (kTileBytes / 16) + q] = make_uint4(w[r][0], w[r][1], w[r][2], w[r][3]);

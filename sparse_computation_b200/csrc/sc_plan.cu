@@ -20,7 +20,7 @@
 #include "sc_kernels.cuh"
 
 #ifndef SC_DEFAULT_DENSE_MODE
-#define SC_DEFAULT_DENSE_MODE 0
+#define SC_DEFAULT_DENSE_MODE 2
 #endif
 
 namespace {
