@@ -1,5 +1,8 @@
 // Dense-tile tcgen05 kernels (see sc_dense.cuh for the scheme).
 //
+// dense_gemm_persist_kernel (tasks not split over a cluster; described at
+// its definition) and dense_gemm_kernel, one CTA per task:
+//
 // CTA = one 128-row block x one 128-column C tile, 4 warps:
 //   thread 0   producer: per kept K-chunk, bulk-copies the A_hi, A_lo, B_hi,
 //              B_lo tile images (4 x 16 KiB) into a 3-stage ring, completion
