@@ -74,13 +74,15 @@ __device__ __forceinline__ void bulk_copy(void *dst_smem, const void *src, uint3
 
 // tcgen05 shared-memory matrix descriptor: K-major, 128B swizzle, 8-row
 // groups 1024 bytes apart (tile base 1024-byte aligned).
+// SW64: 64-byte swizzle instead, 8-row groups 512 bytes apart (3xBF16 images).
+template <bool SW64 = false>
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   uint64_t d = 0;
-  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address       [0,14)
-  d |= (uint64_t)1 << 16;                     // leading byte offset [16,30) (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;           // stride byte offset  [32,46)
-  d |= (uint64_t)1 << 46;                     // descriptor version  [46,48)
-  d |= (uint64_t)2 << 61;                     // SWIZZLE_128B        [61,64)
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);           // start address       [0,14)
+  d |= (uint64_t)1 << 16;                              // leading byte offset [16,30) (unused for swizzled K-major)
+  d |= (uint64_t)((SW64 ? 512 : 1024) >> 4) << 32;     // stride byte offset  [32,46)
+  d |= (uint64_t)1 << 46;                              // descriptor version  [46,48)
+  d |= (uint64_t)(SW64 ? 4 : 2) << 61;                 // SWIZZLE_64B / SWIZZLE_128B [61,64)
   return d;
 }
 
@@ -135,6 +137,52 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// The MMAs of one stage (one kept K-chunk) into the accumulator at `acc`;
+// `first`: the stage starts the accumulator.
+template <int MODE>
+__device__ __forceinline__ void mma_stage(uint32_t acc, uint32_t base, bool first) {
+  if constexpr (MODE == kModeBf16x3) {
+    constexpr int TB = mode_tile_bytes(kModeBf16x3);
+    uint64_t a[3], b[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      a[j] = sdesc<true>(base + j * TB);
+      b[j] = sdesc<true>(base + (3 + j) * TB);
+    }
+#pragma unroll
+    for (int k = 0; k < kBKx3 / 16; ++k) {
+      const uint64_t step = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
+      mma_bf16(acc, a[2] + step, b[0] + step, (!first || k > 0) ? 1u : 0u);
+      mma_bf16(acc, a[0] + step, b[2] + step, 1u);
+      mma_bf16(acc, a[1] + step, b[1] + step, 1u);
+      mma_bf16(acc, a[1] + step, b[0] + step, 1u);
+      mma_bf16(acc, a[0] + step, b[1] + step, 1u);
+      mma_bf16(acc, a[0] + step, b[0] + step, 1u);
+    }
+  } else if constexpr (MODE == kModeBf16) {
+    const uint64_t a = sdesc(base), b = sdesc(base + kTileBytes);
+#pragma unroll
+    for (int k = 0; k < kBKb / 16; ++k) {
+      const uint64_t step = (uint64_t)((k * 32) >> 4);
+      mma_bf16(acc, a + step, b + step, (!first || k > 0) ? 1u : 0u);
+    }
+  } else {
+    const uint64_t a_hi = sdesc(base), a_lo = sdesc(base + kTileBytes);
+    const uint64_t b_hi = sdesc(base + 2 * kTileBytes), b_lo = sdesc(base + 3 * kTileBytes);
+#pragma unroll
+    for (int k = 0; k < kBK / 8; ++k) {
+      const uint64_t step = (uint64_t)((k * 32) >> 4);
+      mma_tf32(acc, a_lo + step, b_hi + step, (!first || k > 0) ? 1u : 0u);
+      mma_tf32(acc, a_hi + step, b_lo + step, 1u);
+      mma_tf32(acc, a_hi + step, b_hi + step, 1u);
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // Sum of the partial accumulators of a cluster of S CTAs (split K): warp w's
 // TMEM rows (C rows 32w..32w+31 of the tile) are owned by CTA w / (4/S); the
 // other CTAs send theirs into the owner's shared memory (slots of 32 rows x
@@ -145,10 +193,9 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
                   int *status) {
   // tf32 x3: stage = A_hi, A_lo, B_hi, B_lo (64 KiB), 3 stages;
   // bf16:    stage = A, B (32 KiB), 6 stages;
-  // bf16 x3: stage = A1, A2, A3, B1, B2, B3 (96 KiB), 2 stages.
-  constexpr bool BF16 = MODE != kModeTf32x3;
-  constexpr int NST = MODE == kModeBf16 ? 6 : (MODE == kModeBf16x3 ? 2 : kStages);
-  constexpr int SB = 2 * mode_images(MODE) * kTileBytes;
+  // bf16 x3: stage = A1, A2, A3, B1, B2, B3 (48 KiB, 32-wide K), 4 stages.
+  constexpr int NST = mode_stages(MODE);
+  constexpr int SB = 2 * mode_images(MODE) * mode_tile_bytes(MODE);
   extern __shared__ __align__(1024) uint8_t dsmem[];
   // 1024-byte aligned stage ring (the swizzle is applied on address bits).
   uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
@@ -191,7 +238,7 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
 
   if (threadIdx.x == 0 && nk > 0 && !m.starve) {
     // producer
-    constexpr int OP = mode_images(MODE) * kTileBytes;  // bytes of one operand's images
+    constexpr int OP = mode_images(MODE) * mode_tile_bytes(MODE);  // bytes of one operand's images
     for (int i = 0; i < nk; ++i) {
       const int s = i % NST;
       if (i >= NST && !mbar_wait(&empty_bar[s], ((i / NST) - 1) & 1, &abort_flag)) {
@@ -220,43 +267,7 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
         break;
       }
       tc_fence_after();
-      const uint32_t base = smem_u32(ring + (size_t)s * SB);
-      if constexpr (MODE == kModeBf16x3) {
-        uint64_t a[3], b[3];
-#pragma unroll
-        for (int j = 0; j < 3; ++j) {
-          a[j] = sdesc(base + j * kTileBytes);
-          b[j] = sdesc(base + (3 + j) * kTileBytes);
-        }
-#pragma unroll
-        for (int k = 0; k < kBKb / 16; ++k) {
-          const uint64_t step = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
-          // smallest terms first; the first MMA of a tile starts the accumulator
-          mma_bf16(tmem, a[2] + step, b[0] + step, (i > 0 || k > 0) ? 1u : 0u);
-          mma_bf16(tmem, a[0] + step, b[2] + step, 1u);
-          mma_bf16(tmem, a[1] + step, b[1] + step, 1u);
-          mma_bf16(tmem, a[1] + step, b[0] + step, 1u);
-          mma_bf16(tmem, a[0] + step, b[1] + step, 1u);
-          mma_bf16(tmem, a[0] + step, b[0] + step, 1u);
-        }
-      } else if constexpr (BF16) {
-        const uint64_t a = sdesc(base), b = sdesc(base + kTileBytes);
-#pragma unroll
-        for (int k = 0; k < kBKb / 16; ++k) {
-          const uint64_t step = (uint64_t)((k * 32) >> 4);  // 16 bf16 = 32 bytes along K
-          mma_bf16(tmem, a + step, b + step, (i > 0 || k > 0) ? 1u : 0u);
-        }
-      } else {
-        const uint64_t a_hi = sdesc(base), a_lo = sdesc(base + kTileBytes);
-        const uint64_t b_hi = sdesc(base + 2 * kTileBytes), b_lo = sdesc(base + 3 * kTileBytes);
-#pragma unroll
-        for (int k = 0; k < kBK / 8; ++k) {
-          const uint64_t step = (uint64_t)((k * 32) >> 4);  // 8 tf32 = 32 bytes along K
-          mma_tf32(tmem, a_lo + step, b_hi + step, (i > 0 || k > 0) ? 1u : 0u);
-          mma_tf32(tmem, a_hi + step, b_lo + step, 1u);
-          mma_tf32(tmem, a_hi + step, b_hi + step, 1u);
-        }
-      }
+      mma_stage<MODE>(tmem, smem_u32(ring + (size_t)s * SB), i == 0);
       mma_commit(&empty_bar[s]);  // stage free once these MMAs have read it
     }
     if (ok) mma_commit(&done_bar);
@@ -339,51 +350,6 @@ dense_gemm_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *_
   }
 }
 
-// The MMAs of one stage (one kept K-chunk) into the accumulator at `acc`;
-// `first`: the stage starts the accumulator.
-template <int MODE>
-__device__ __forceinline__ void mma_stage(uint32_t acc, uint32_t base, bool first) {
-  if constexpr (MODE == kModeBf16x3) {
-    uint64_t a[3], b[3];
-#pragma unroll
-    for (int j = 0; j < 3; ++j) {
-      a[j] = sdesc(base + j * kTileBytes);
-      b[j] = sdesc(base + (3 + j) * kTileBytes);
-    }
-#pragma unroll
-    for (int k = 0; k < kBKb / 16; ++k) {
-      const uint64_t step = (uint64_t)((k * 32) >> 4);
-      mma_bf16(acc, a[2] + step, b[0] + step, (!first || k > 0) ? 1u : 0u);
-      mma_bf16(acc, a[0] + step, b[2] + step, 1u);
-      mma_bf16(acc, a[1] + step, b[1] + step, 1u);
-      mma_bf16(acc, a[1] + step, b[0] + step, 1u);
-      mma_bf16(acc, a[0] + step, b[1] + step, 1u);
-      mma_bf16(acc, a[0] + step, b[0] + step, 1u);
-    }
-  } else if constexpr (MODE == kModeBf16) {
-    const uint64_t a = sdesc(base), b = sdesc(base + kTileBytes);
-#pragma unroll
-    for (int k = 0; k < kBKb / 16; ++k) {
-      const uint64_t step = (uint64_t)((k * 32) >> 4);
-      mma_bf16(acc, a + step, b + step, (!first || k > 0) ? 1u : 0u);
-    }
-  } else {
-    const uint64_t a_hi = sdesc(base), a_lo = sdesc(base + kTileBytes);
-    const uint64_t b_hi = sdesc(base + 2 * kTileBytes), b_lo = sdesc(base + 3 * kTileBytes);
-#pragma unroll
-    for (int k = 0; k < kBK / 8; ++k) {
-      const uint64_t step = (uint64_t)((k * 32) >> 4);
-      mma_tf32(acc, a_lo + step, b_hi + step, (!first || k > 0) ? 1u : 0u);
-      mma_tf32(acc, a_hi + step, b_lo + step, 1u);
-      mma_tf32(acc, a_hi + step, b_hi + step, 1u);
-    }
-  }
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // Persistent form for tasks not split over a cluster: one CTA per SM.  Its
 // producer thread takes task tickets from a counter in global memory
 // (status[1]; heaviest tasks first, so SMs that finish early take more) and
@@ -403,9 +369,9 @@ template <bool BATCH, int MODE>
 __global__ void __launch_bounds__(kPersistThreads, 1)
 dense_gemm_persist_kernel(DenseMat one, const DenseMat *__restrict__ mats, const int4 *__restrict__ tasks,
                           int64_t ntasks, int accumulate, int *status) {
-  constexpr int NST = MODE == kModeBf16 ? 6 : (MODE == kModeBf16x3 ? 2 : kStages);
-  constexpr int SB = 2 * mode_images(MODE) * kTileBytes;
-  constexpr int OP = mode_images(MODE) * kTileBytes;  // bytes of one operand's images
+  constexpr int NST = mode_stages(MODE);
+  constexpr int SB = 2 * mode_images(MODE) * mode_tile_bytes(MODE);
+  constexpr int OP = mode_images(MODE) * mode_tile_bytes(MODE);  // bytes of one operand's images
   extern __shared__ __align__(1024) uint8_t dsmem[];
   uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[NST], empty_bar[NST], acc_full[2], acc_empty[2], done_bar;
@@ -691,24 +657,27 @@ __global__ void __launch_bounds__(256) split_b_bf16_kernel(DenseMat one, const D
   }
 }
 
-// bf16 x3 mode: three images (x1, x2, x3 parts) per (n tile, 64-wide K chunk).
+// bf16 x3 mode: three images (x1, x2, x3 parts) per (n tile, 32-wide K chunk),
+// 64-byte swizzled rows.
 template <bool BATCH>
 __global__ void __launch_bounds__(256) split_b_bf16x3_kernel(DenseMat one, const DenseMat *__restrict__ mats) {
-  __shared__ float T[kBKb][kBN + 1];
+  constexpr int TB = mode_tile_bytes(kModeBf16x3);
+  __shared__ float T[kBKx3][kBN + 1];
   DenseMat m;
   if constexpr (BATCH) m = mats[blockIdx.y];
   else m = one;
   const int tile = blockIdx.x;
   if (tile >= m.n_tiles * m.k_chunks) return;
   const int nt = tile / m.k_chunks, kc = tile % m.k_chunks;
-  load_b_chunk<kBKb>(m, nt, kc, T);
+  load_b_chunk<kBKx3>(m, nt, kc, T);
   __syncthreads();
-  uint4 *img = reinterpret_cast<uint4 *>(m.b_tiles + ((size_t)nt * m.k_chunks + kc) * 3 * kTileBytes);
-  for (int q = threadIdx.x; q < kBN * 8; q += blockDim.x) {
-    const int n = q >> 3, c = q & 7;
-    const int k0 = (c ^ (n & 7)) << 3;
-    // the same three parts as bf16x3_split (round to nearest even at each
-    // step), from the hardware conversion: two values per instruction
+  uint4 *img = reinterpret_cast<uint4 *>(m.b_tiles + ((size_t)nt * m.k_chunks + kc) * 3 * TB);
+  // 16-byte chunk q: row n = q / 4, physical chunk c = q % 4 holding logical
+  // k = 8 * (c ^ ((n >> 1) & 3)) .. +7; the parts from the hardware bf16
+  // conversion (round to nearest even at each step, as bf16x3_split)
+  for (int q = threadIdx.x; q < kBN * 4; q += blockDim.x) {
+    const int n = q >> 2, c = q & 3;
+    const int k0 = (c ^ ((n >> 1) & 3)) << 3;
     uint32_t w[3][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -727,7 +696,7 @@ __global__ void __launch_bounds__(256) split_b_bf16x3_kernel(DenseMat one, const
       w[2][j] = *reinterpret_cast<const uint32_t *>(&p3);
     }
 #pragma unroll
-    for (int r = 0; r < 3; ++r) img[r * (kTileBytes / 16) + q] = make_uint4(w[r][0], w[r][1], w[r][2], w[r][3]);
+    for (int r = 0; r < 3; ++r) img[r * (TB / 16) + q] = make_uint4(w[r][0], w[r][1], w[r][2], w[r][3]);
   }
 }
 

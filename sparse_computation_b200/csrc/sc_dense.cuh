@@ -72,7 +72,21 @@ constexpr int kModeTf32x3 = 0;
 constexpr int kModeBf16 = 1;
 constexpr int kModeBf16x3 = 2;
 __host__ __device__ constexpr int mode_images(int mode) { return mode == kModeBf16 ? 1 : (mode == kModeBf16x3 ? 3 : 2); }
-__host__ __device__ constexpr int mode_bk(int mode) { return mode == kModeTf32x3 ? kBK : kBKb; }
+// 3xBF16 stages hold 32-wide K chunks in 64-byte swizzled rows (six 8 KiB
+// images, 48 KiB a stage, four stages); the other modes 128-byte rows.
+constexpr int kBKx3 = 32;
+__host__ __device__ constexpr int mode_bk(int mode) {
+  return mode == kModeTf32x3 ? kBK : (mode == kModeBf16x3 ? kBKx3 : kBKb);
+}
+__host__ __device__ constexpr int mode_tile_bytes(int mode) { return mode == kModeBf16x3 ? kTileBytes / 2 : kTileBytes; }
+__host__ __device__ constexpr int mode_stages(int mode) { return mode == kModeBf16 ? 6 : (mode == kModeBf16x3 ? 4 : kStages); }
+
+// 64-byte swizzle (3xBF16 images): row r of 64 bytes, 16-byte chunk c stored
+// at c ^ ((r >> 1) & 3) -- byte address bits [4,6) xor bits [7,9).
+__host__ __device__ inline uint32_t swz_offset_bf16_64(int r, int k) {
+  const uint32_t chunk = (uint32_t)(k >> 3) ^ (uint32_t)((r >> 1) & 3);
+  return (uint32_t)r * 64u + chunk * 16u + (uint32_t)(k & 7) * 2u;
+}
 
 __host__ __device__ inline uint32_t swz_offset_bf16(int r, int k) {
   const uint32_t chunk = (uint32_t)(k >> 3) ^ (uint32_t)(r & 7);

@@ -346,7 +346,8 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
       if (!any) continue;
       rb_chunk.push_back(kc);
       const size_t off = tiles.size();
-      tiles.resize(off + (size_t)images * kTileBytes, 0);
+      const size_t tb = (size_t)mode_tile_bytes(mode);
+      tiles.resize(off + (size_t)images * tb, 0);
       for (int r = 0; r < kBM; ++r)
         for (int k = 0; k < bk; ++k) {
           const int64_t gk = (int64_t)kc * bk + k;
@@ -354,7 +355,7 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
           if (mode == kModeBf16x3) {
             uint16_t h[3];
             bf16x3_split(x, h);
-            for (int j = 0; j < 3; ++j) memcpy(&tiles[off + j * kTileBytes + swz_offset_bf16(r, k)], &h[j], 2);
+            for (int j = 0; j < 3; ++j) memcpy(&tiles[off + j * tb + swz_offset_bf16_64(r, k)], &h[j], 2);
           } else if (mode == kModeBf16) {
             const uint16_t h = bf16_bits(x);
             memcpy(&tiles[off + swz_offset_bf16(r, k)], &h, 2);
@@ -368,7 +369,7 @@ void build_dense(sc_plan &p, const sc_cf &cf, int64_t pb, const std::vector<int>
     rb_ptr[b + 1] = (int32_t)rb_chunk.size();
   }
   const int nts = (int)(p.n / kBN);
-  const size_t b_bytes = (size_t)nts * kcs * images * kTileBytes;
+  const size_t b_bytes = (size_t)nts * kcs * images * mode_tile_bytes(mode);
   std::vector<int4> tasks;
   for (int64_t b = 0; b < rbs; ++b)
     for (int t = 0; t < nts; ++t) tasks.push_back(make_int4(0, (int)b, t, rb_ptr[b + 1] - rb_ptr[b]));
