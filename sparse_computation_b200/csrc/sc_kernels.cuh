@@ -956,8 +956,10 @@ __device__ __forceinline__ void dispatch_lane(int P, const LaneBuf &b, const flo
   }
 }
 
-// Lane blocks with B read through L1 (N = 4, or a layout forced by
-// SC_NARROW_LAYOUT=lane): same arguments, grid and result as
+// Lane blocks with B read through L1 (only when SC_NARROW_LAYOUT=lane forces
+// the layout on a plan the staged kernel does not take; measured 31.7 us on
+// the config-5 SpMV against 30.7 us for split blocks): same arguments, grid
+// and result as
 // spmm_narrow_kernel; each warp loads its next item before it gathers the B
 // rows of the current one.
 template <int KM, int NB>
