@@ -303,6 +303,29 @@ def test_staged_small_b_kernel_m_sweep(cuda):
         assert np.all(np.abs(y2 - ref) <= RTOL * scale), km
 
 
+def test_staged_spmv_host_entry_point(cuda):
+    """The host entry point on a plan that takes the staged SpMV kernel:
+    pageable buffers (row chunks, each a subset of the panel order) and
+    page-locked ones (C stored straight into host memory) both match the
+    oracle at the fp32 bound, twice in a row."""
+    import torch
+    from sparse_computation_b200.partition import row_slice
+    a, B = wl.config5(n_cols_b=1)
+    a = row_slice(a, 0, 6144)
+    _, _, ip, ix, dx = a
+    ref = cpu.spmm_csr_float(ip, ix, dx, B)
+    scale = cpu.spmm_csr_abs(ip, ix, dx, B)
+    plan = sc.SpMMPlan(sc.csr_to_compressed_format_converter(to_csr_handle(a), 4, 1), 1)
+    hB = torch.from_numpy(B).pin_memory()
+    hC = torch.full((a[0], 1), float("nan")).pin_memory()
+    for _ in range(2):
+        y = plan.spmm_host(B).astype(np.float64)
+        assert np.all(np.abs(y - ref) <= RTOL * scale)
+        plan.spmm_host(hB.numpy(), hC.numpy())
+        assert np.all(np.abs(hC.numpy().astype(np.float64) - ref) <= RTOL * scale)
+    assert plan.status() == 0
+
+
 def test_batch_layer_stack_one_launch(cuda):
     """All 96 weights of config 4 in one launch == the oracle for each."""
     import torch
